@@ -1,0 +1,174 @@
+"""ctypes binding of ``libdwconv_b200.so``, the engine's C ABI (include/dwconv_b200.h).
+
+The library is built in-tree by ``depthwise_conv_b200/csrc/build.py``.  There
+is no fallback: if the library is missing or cannot be loaded, every entry
+point raises ``RuntimeError`` naming the problem.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG_DIR, "libdwconv_b200.so")
+
+# dwb_status
+OK = 0
+ERR_NULL_POINTER = 1
+ERR_BAD_SHAPE = 2
+ERR_BAD_ALIGN = 3
+ERR_UNSUPPORTED = 4
+ERR_CUDA = 5
+ERR_NO_DEVICE = 6
+ERR_DEVICE_TIMEOUT = 7
+ERR_BAD_ARG = 8
+
+# dwb_act / dwb_accum
+ACT_NONE, ACT_RELU, ACT_GELU = 0, 1, 2
+ACT_CODES = {"none": ACT_NONE, "relu": ACT_RELU, "gelu": ACT_GELU}
+ACCUM_F32, ACCUM_MIXED = 0, 1
+
+# Every entry point the header declares, with its ctypes signature.
+_p, _i, _i64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
+
+
+class Problem(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int64), ("height", ctypes.c_int64), ("width", ctypes.c_int64),
+                ("channels", ctypes.c_int64), ("kernel_size", ctypes.c_int32), ("accum", ctypes.c_int32)]
+
+
+class Plan(ctypes.Structure):
+    _fields_ = [("kernel_size", ctypes.c_int32), ("cols_per_thread", ctypes.c_int32),
+                ("rows_per_thread", ctypes.c_int32), ("channel_block", ctypes.c_int32),
+                ("tile_h", ctypes.c_int32), ("tile_w", ctypes.c_int32), ("tile_w_in", ctypes.c_int32),
+                ("ring_rows", ctypes.c_int32), ("ring_wrows", ctypes.c_int32), ("consumer_warps", ctypes.c_int32),
+                ("threads", ctypes.c_int32), ("smem_bytes", ctypes.c_int32), ("ctas_per_sm", ctypes.c_int32),
+                ("grid", ctypes.c_int64), ("accum", ctypes.c_int32), ("regs_estimate", ctypes.c_int32),
+                ("model_cost", ctypes.c_double)]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "Plan":
+        p = cls()
+        for name, _ in cls._fields_:
+            if name in d:
+                setattr(p, name, d[name])
+        return p
+
+
+SIGNATURES = {
+    "dwb_abi_version": ([], _i),
+    "dwb_status_string": ([_i], ctypes.c_char_p),
+    "dwb_plan_query": ([ctypes.POINTER(Problem), _i, _i, ctypes.POINTER(Plan)], _i),
+    "dwb_plan_candidates": ([ctypes.POINTER(Problem), _i, _i, ctypes.POINTER(Plan), _i, ctypes.POINTER(_i)], _i),
+    "dwb_last_error": ([], ctypes.c_char_p),
+    "dwb_conv2d_nhwc_fwd_planned": ([_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i, _i,
+                                     ctypes.POINTER(Plan), _p], _i),
+    "dwb_conv2d_nhwc_fwd": ([_p, _p, _p, _i64, _i64, _i64, _i64, _i, _p], _i),
+    "dwb_conv2d_nhwc_fused_fwd": ([_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i, _i, _i, _p], _i),
+    "dwb_depthwise_forward_32_768_7": ([_p, _p, _p, _i, _i, _i, _i, _i, _p], _i),
+    "dwb_depthwise_forward_32_1536_9": ([_p, _p, _p, _i, _i, _i, _i, _i, _i, _p], _i),
+    "dwb_depthwise_forward_32_1536_9_v2": ([_p, _p, _p, _i, _i, _i, _i, _i, _i, _p], _i),
+    "dwb_depthwise_forward_16_1536_9": ([_p, _p, _p, _i, _i, _i, _i, _i, _p], _i),
+    "dwb_depthwise_forward_32_1536_13": ([_p, _p, _p, _i, _i, _i, _i, _i, _p], _i),
+    "dwb_depthwise_31x31_128_nhwc": ([_p, _p, _p, _p, _i, _i, _i, _i, _p], _i),
+    "dwb_depthwise_29x29_256_nhwc": ([_p, _p, _p, _p, _i, _i, _i, _i, _p], _i),
+    "dwb_depthwise_27x27_512_nhwc": ([_p, _p, _p, _p, _i, _i, _i, _i, _p], _i),
+    "dwb_device_error": ([ctypes.POINTER(ctypes.c_int), _i, _p], _i),
+    "dwb_probe_fma_peak": ([ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double), _p], _i),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+class DwbError(RuntimeError):
+    """A non-OK status returned by the engine's C ABI."""
+
+    def __init__(self, fn: str, status: int):
+        self.status = status
+        detail = ""
+        if status == ERR_CUDA:
+            try:
+                detail = ": " + load().dwb_last_error().decode()
+            except Exception:  # pragma: no cover
+                pass
+        super().__init__(f"{fn} failed: status {status} ({status_string(status)}){detail}")
+
+
+def load() -> ctypes.CDLL:
+    """Load the C-ABI library (once).  Raises RuntimeError if it is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"depthwise_conv_b200: CUDA library {LIB_PATH} is missing; build it with "
+                    "`python -m depthwise_conv_b200.csrc.build` (there is no CPU fallback)")
+            lib = ctypes.CDLL(LIB_PATH)
+            for name, (argtypes, restype) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = argtypes
+                fn.restype = restype
+            if lib.dwb_abi_version() != 1:
+                raise RuntimeError("depthwise_conv_b200: ABI version mismatch")
+            _lib = lib
+    return _lib
+
+
+def status_string(status: int) -> str:
+    try:
+        return load().dwb_status_string(status).decode()
+    except Exception:  # pragma: no cover - library absent
+        return "unknown"
+
+
+def check(fn: str, status: int) -> None:
+    if status != OK:
+        raise DwbError(fn, status)
+
+
+def call(fn: str, *args) -> None:
+    """Call an entry point and raise DwbError on a non-OK status."""
+    check(fn, getattr(load(), fn)(*args))
+
+
+def plan_query(B: int, H: int, W: int, C: int, K: int, accum: int = ACCUM_F32, sm_count: int = 0,
+               smem_optin: int = 0) -> dict:
+    """The planner's choice for a problem (host arithmetic only, no GPU needed)."""
+    pr = Problem(B, H, W, C, K, accum)
+    out = Plan()
+    check("dwb_plan_query", load().dwb_plan_query(ctypes.byref(pr), sm_count, smem_optin, ctypes.byref(out)))
+    return out.as_dict()
+
+
+def plan_candidates(B: int, H: int, W: int, C: int, K: int, accum: int = ACCUM_F32, sm_count: int = 0,
+                    smem_optin: int = 0) -> list[dict]:
+    """Every feasible plan of a problem with its modelled cost (host arithmetic only)."""
+    pr = Problem(B, H, W, C, K, accum)
+    n = ctypes.c_int(0)
+    check("dwb_plan_candidates", load().dwb_plan_candidates(ctypes.byref(pr), sm_count, smem_optin, None, 0,
+                                                            ctypes.byref(n)))
+    arr = (Plan * max(1, n.value))()
+    check("dwb_plan_candidates", load().dwb_plan_candidates(ctypes.byref(pr), sm_count, smem_optin, arr, n.value,
+                                                            ctypes.byref(n)))
+    return [arr[i].as_dict() for i in range(n.value)]
+
+
+def device_error(stream: int = 0, clear: bool = True) -> int:
+    """Device error word (0 = no bounded wait has expired); synchronises ``stream``."""
+    code = ctypes.c_int(0)
+    check("dwb_device_error", load().dwb_device_error(ctypes.byref(code), int(clear), stream))
+    return code.value
+
+
+def probe_fma_peak(stream: int = 0) -> tuple[float, float]:
+    """Measured (HFMA2, FFMA2) CUDA-core rates of the current device, TFLOP/s."""
+    a, b = ctypes.c_double(0.0), ctypes.c_double(0.0)
+    check("dwb_probe_fma_peak", load().dwb_probe_fma_peak(ctypes.byref(a), ctypes.byref(b), stream))
+    return a.value, b.value

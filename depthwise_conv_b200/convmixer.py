@@ -1,0 +1,127 @@
+"""ConvMixer host model for the end-to-end metric, with the engine's fused DW block.
+
+The network follows the reference's ``convmixer/convmixer.py`` layer for
+layer (``ConvMixerWrapper`` :62-161, configs :17-42): patch conv -> act ->
+BN, then ``depth`` blocks of [Residual(DW conv -> act -> BN) -> 1x1 conv ->
+act -> BN], then avg-pool, flatten, linear.  Weights are random, initialised
+as the benchmark configuration prescribes (no checkpoints are involved):
+conv/linear weights N(0, 0.02), biases 0, BN gamma=1 beta=0, running mean 0,
+running var 1.
+
+``fuse_dw_blocks`` swaps each Residual(DW conv, act, BN) for one
+``depthwise::conv2d_nhwc_fused`` call that computes
+``act(conv(x) + b) * s + t + x`` in a single kernel, with s, t the
+inference-mode BN fold (benchmark_cudnn_fused_e2e.py:115-134, :125-131).
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from . import dw_ops  # noqa: F401  (registers depthwise::conv2d_nhwc_fused)
+
+CONVMIXER_MODELS = {
+    '768_32': {'dim': 768, 'depth': 32, 'kernel_size': 7, 'patch_size': 7, 'activation': 'relu', 'n_classes': 1000},
+    '1024_20': {'dim': 1024, 'depth': 20, 'kernel_size': 9, 'patch_size': 14, 'activation': 'gelu',
+                'n_classes': 1000},
+    '1536_20': {'dim': 1536, 'depth': 20, 'kernel_size': 9, 'patch_size': 7, 'activation': 'gelu',
+                'n_classes': 1000},
+}
+
+
+class Residual(nn.Module):
+    def __init__(self, fn):
+        super().__init__()
+        self.fn = fn
+
+    def forward(self, x):
+        return self.fn(x) + x
+
+
+class ConvMixer(nn.Module):
+    """Same Sequential indexing as the reference's ConvMixerWrapper (convmixer/convmixer.py:93-127)."""
+
+    def __init__(self, dim, depth, kernel_size=9, patch_size=7, n_classes=1000, activation='gelu'):
+        super().__init__()
+        self.dim, self.depth, self.kernel_size = dim, depth, kernel_size
+        self.patch_size, self.n_classes, self.activation = patch_size, n_classes, activation
+        act_fn = nn.ReLU if activation == 'relu' else nn.GELU
+        layers = [nn.Conv2d(3, dim, kernel_size=patch_size, stride=patch_size), act_fn(), nn.BatchNorm2d(dim)]
+        for _ in range(depth):
+            layers.append(nn.Sequential(
+                Residual(nn.Sequential(
+                    nn.Conv2d(dim, dim, kernel_size, groups=dim, padding='same'),
+                    act_fn(),
+                    nn.BatchNorm2d(dim))),
+                nn.Conv2d(dim, dim, kernel_size=1),
+                act_fn(),
+                nn.BatchNorm2d(dim)))
+        layers += [nn.AdaptiveAvgPool2d((1, 1)), nn.Flatten(), nn.Linear(dim, n_classes)]
+        self.model = nn.Sequential(*layers)
+
+    def forward(self, x):
+        if not x.is_contiguous(memory_format=torch.channels_last):
+            x = x.contiguous(memory_format=torch.channels_last)
+        return self.model(x)
+
+
+def init_baseline_(model: nn.Module, seed: int = 0) -> nn.Module:
+    """Random init of the benchmark configuration (seeded, CPU generator)."""
+    g = torch.Generator().manual_seed(seed)
+    with torch.no_grad():
+        for m in model.modules():
+            if isinstance(m, (nn.Conv2d, nn.Linear)):
+                m.weight.copy_(torch.randn(m.weight.shape, generator=g) * 0.02)
+                if m.bias is not None:
+                    m.bias.zero_()
+            elif isinstance(m, nn.BatchNorm2d):
+                m.weight.fill_(1.0)
+                m.bias.zero_()
+                m.running_mean.zero_()
+                m.running_var.fill_(1.0)
+    return model
+
+
+def convmixer(name: str, seed: int = 0) -> ConvMixer:
+    cfg = CONVMIXER_MODELS[name]
+    return init_baseline_(ConvMixer(**cfg), seed).eval()
+
+
+class FusedDWBlock(nn.Module):
+    """Residual(DW conv -> act -> BN) as one engine kernel: act(conv(x) + b) * s + t + x."""
+
+    def __init__(self, conv: nn.Conv2d, act: str, bn: nn.BatchNorm2d):
+        super().__init__()
+        C = conv.in_channels
+        self.act = act
+        with torch.no_grad():
+            w = conv.weight.detach().squeeze(1).permute(1, 2, 0).contiguous().half()  # [K,K,C]
+            b = conv.bias.detach().half() if conv.bias is not None else torch.zeros(C, dtype=torch.float16)
+            scale = bn.weight / torch.sqrt(bn.running_var + bn.eps)
+            shift = bn.bias - bn.running_mean * scale
+        self.register_buffer("weight", w)
+        self.register_buffer("bias", b.contiguous())
+        self.register_buffer("scale", scale.half().contiguous())
+        self.register_buffer("shift", shift.half().contiguous())
+        self.act_code = dw_ops.ACT_CODES[act]
+
+    def forward(self, x):
+        return torch.ops.depthwise.conv2d_nhwc_fused(x, self.weight, self.bias, self.scale, self.shift, x,
+                                                     self.act_code)
+
+
+def fuse_dw_blocks(model: ConvMixer) -> ConvMixer:
+    """Replace every Residual(DW conv, act, BN) of a ConvMixer with a FusedDWBlock."""
+    n = 0
+    for block in model.model:
+        if not isinstance(block, nn.Sequential):
+            continue
+        for i, sub in enumerate(block):
+            if isinstance(sub, Residual) and isinstance(sub.fn, nn.Sequential) and len(sub.fn) == 3:
+                conv, act, bn = sub.fn
+                if isinstance(conv, nn.Conv2d) and conv.groups == conv.in_channels == conv.out_channels:
+                    act_name = 'relu' if isinstance(act, nn.ReLU) else 'gelu'
+                    block[i] = FusedDWBlock(conv, act_name, bn).to(conv.weight.device)
+                    n += 1
+    model.fused_blocks = n
+    return model

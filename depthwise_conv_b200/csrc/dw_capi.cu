@@ -1,0 +1,521 @@
+// dw_capi.cu -- the C ABI of the engine (include/dwconv_b200.h): argument
+// validation, planning, TMA descriptor encoding and kernel launch.
+//
+// Nothing here allocates device memory, synchronises (except the explicit
+// diagnostics call) or launches on any stream but the caller's.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "../../include/dwconv_b200.h"
+#include "dw_kernel.cuh"
+#include "dw_planner.h"
+
+namespace dwb {
+
+// ---- variant registry --------------------------------------------------------
+#define DWB_DECLARE_TABLE(K)             \
+  extern const KernelEntry kTableK##K[]; \
+  extern const int kCountK##K;
+DWB_DECLARE_TABLE(1)
+DWB_DECLARE_TABLE(3)
+DWB_DECLARE_TABLE(5)
+DWB_DECLARE_TABLE(7)
+DWB_DECLARE_TABLE(9)
+DWB_DECLARE_TABLE(11)
+DWB_DECLARE_TABLE(13)
+DWB_DECLARE_TABLE(15)
+DWB_DECLARE_TABLE(17)
+DWB_DECLARE_TABLE(19)
+DWB_DECLARE_TABLE(21)
+DWB_DECLARE_TABLE(23)
+DWB_DECLARE_TABLE(25)
+DWB_DECLARE_TABLE(27)
+DWB_DECLARE_TABLE(29)
+DWB_DECLARE_TABLE(31)
+
+int kernels_for_k(int K, const KernelEntry** out) {
+  switch (K) {
+#define DWB_CASE(KK)       \
+  case KK:                 \
+    *out = kTableK##KK;    \
+    return kCountK##KK;
+    DWB_CASE(1) DWB_CASE(3) DWB_CASE(5) DWB_CASE(7) DWB_CASE(9) DWB_CASE(11) DWB_CASE(13) DWB_CASE(15)
+    DWB_CASE(17) DWB_CASE(19) DWB_CASE(21) DWB_CASE(23) DWB_CASE(25) DWB_CASE(27) DWB_CASE(29) DWB_CASE(31)
+#undef DWB_CASE
+    default:
+      *out = nullptr;
+      return 0;
+  }
+}
+
+static const KernelEntry* find_variant(int K, int R, int M, int acc) {
+  const KernelEntry* tab = nullptr;
+  const int n = kernels_for_k(K, &tab);
+  for (int i = 0; i < n; ++i)
+    if (tab[i].r == R && tab[i].m == M && tab[i].acc == acc) return &tab[i];
+  return nullptr;
+}
+
+// ---- per-device state -----------------------------------------------------------
+// The device error word: written by kernels whose bounded waits expire.
+static __device__ int g_device_error;
+
+constexpr int kMaxDevices = 64;
+constexpr int kMaxVariants = 16 * 16;  // K values x variants per K
+
+struct VariantState {
+  int regs = -1;         // -1 unknown, 0 unavailable
+  bool smem_set = false;
+  int smem_max = 0;
+};
+
+using PlanKey = std::tuple<long long, long long, long long, long long, int, int>;  // B, H, W, C, K, accum
+
+struct DeviceState {
+  std::once_flag once;
+  int status = DWB_ERR_NO_DEVICE;
+  HwInfo hw;
+  int* err_word = nullptr;
+  std::mutex mu;
+  VariantState variants[kMaxVariants];
+  std::mutex plan_mu;
+  std::map<PlanKey, dwb_plan> plans;  // planner results, computed once per problem
+};
+
+// Last CUDA failure of this thread, for dwb_last_error().
+static thread_local char g_last_error[256] = "";
+
+static int cuda_fail(const char* what, cudaError_t e) {
+  std::snprintf(g_last_error, sizeof(g_last_error), "%s: %s (%d)", what, cudaGetErrorString(e), static_cast<int>(e));
+  return DWB_ERR_CUDA;
+}
+
+static int driver_fail(const char* what, int code) {
+  std::snprintf(g_last_error, sizeof(g_last_error), "%s: CUresult %d", what, code);
+  return DWB_ERR_CUDA;
+}
+
+static DeviceState g_devices[kMaxDevices];
+
+static int variant_slot(int K, int R, int M, int acc) {
+  int ri = 0;
+  for (; ri < 4; ++ri)
+    if (kVariantR[ri] == R) break;
+  const int mi = (M == 2) ? 0 : 1;
+  return ((K / 2) * 16) + (ri * 4) + (mi * 2) + acc;
+}
+
+static void init_device(int dev, DeviceState* st) {
+  int major = 0, minor = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (e != cudaSuccess) {
+    st->status = cuda_fail("cudaDeviceGetAttribute", e);
+    return;
+  }
+  if (major != 10) {  // the library is built for sm_100a only
+    st->status = DWB_ERR_NO_DEVICE;
+    return;
+  }
+  int v = 0;
+  cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+  st->hw.sm_count = v;
+  cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  st->hw.smem_optin = v;
+  cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+  st->hw.smem_per_sm = v;
+  cudaDeviceGetAttribute(&v, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+  st->hw.smem_reserved = v;
+  cudaDeviceGetAttribute(&v, cudaDevAttrMaxRegistersPerMultiprocessor, dev);
+  st->hw.regs_per_sm = v;
+  cudaDeviceGetAttribute(&v, cudaDevAttrMaxThreadsPerMultiProcessor, dev);
+  st->hw.max_threads_sm = v;
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_device_error);
+  if (e != cudaSuccess) {
+    st->status = cuda_fail("cudaGetSymbolAddress(g_device_error)", e);
+    return;
+  }
+  st->err_word = static_cast<int*>(p);
+  st->status = DWB_OK;
+}
+
+static int get_device_state(DeviceState** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return DWB_ERR_NO_DEVICE;
+  DeviceState* st = &g_devices[dev];
+  std::call_once(st->once, init_device, dev, st);
+  *out = st;
+  return st->status;
+}
+
+static int regs_of_variant(int K, int R, int M, int acc, void* ctx) {
+  DeviceState* st = static_cast<DeviceState*>(ctx);
+  const KernelEntry* e = find_variant(K, R, M, acc);
+  if (!e) return 0;
+  VariantState& vs = st->variants[variant_slot(K, R, M, acc)];
+  std::lock_guard<std::mutex> lk(st->mu);
+  if (vs.regs < 0) {
+    cudaFuncAttributes fa;
+    vs.regs = (cudaFuncGetAttributes(&fa, e->fn) == cudaSuccess) ? fa.numRegs : 0;
+  }
+  return vs.regs;
+}
+
+static int ensure_smem_attr(DeviceState* st, const KernelEntry* e, int smem) {
+  VariantState& vs = st->variants[variant_slot(e->k, e->r, e->m, e->acc)];
+  std::lock_guard<std::mutex> lk(st->mu);
+  if (vs.smem_max >= smem) return DWB_OK;
+  const cudaError_t ce = cudaFuncSetAttribute(e->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (ce != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(MaxDynamicSharedMemorySize)", ce);
+  vs.smem_max = smem;
+  return DWB_OK;
+}
+
+// ---- TMA descriptors ---------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// x: NHWC fp16 viewed as (C, W, H, B); box = 64 channels x tile_w_in columns x 1 row.
+static int encode_x_map(CUtensorMap* m, const void* x, long long B, long long H, long long W, long long C,
+                        int tile_w_in) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return driver_fail("cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)", -1);
+  const cuuint64_t dims[4] = {(cuuint64_t)C, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)(C * 2), (cuuint64_t)(W * C * 2), (cuuint64_t)(H * W * C * 2)};
+  const cuuint32_t box[4] = {(cuuint32_t)kChannelsPerCta, (cuuint32_t)tile_w_in, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(x), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? DWB_OK : driver_fail("cuTensorMapEncodeTiled(x)", static_cast<int>(r));
+}
+
+// w: [K][K][C] fp16 viewed as (C, K, K); box = 64 channels x K taps x 1 row.
+static int encode_w_map(CUtensorMap* m, const void* w, long long C, int K) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return driver_fail("cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)", -1);
+  const cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)K, (cuuint64_t)K};
+  const cuuint64_t strides[2] = {(cuuint64_t)(C * 2), (cuuint64_t)(K * C * 2)};
+  const cuuint32_t box[3] = {(cuuint32_t)kChannelsPerCta, (cuuint32_t)K, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(w), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? DWB_OK : driver_fail("cuTensorMapEncodeTiled(w)", static_cast<int>(r));
+}
+
+static inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Argument checks shared by every entry point (no CUDA calls).  An empty
+// batch is accepted before the pointer checks: an empty tensor may report a
+// null data pointer.
+static int validate_args(const void* x, const void* w, const void* bias, const void* scale, const void* shift,
+                         const void* residual, const void* y, long long B, long long H, long long W, long long C,
+                         int K, int act, int accum) {
+  if (act < DWB_ACT_NONE || act > DWB_ACT_GELU) return DWB_ERR_BAD_ARG;
+  if (accum != DWB_ACCUM_F32 && accum != DWB_ACCUM_MIXED) return DWB_ERR_BAD_ARG;
+  if (B < 0 || H < 1 || W < 1 || C < 1 || K < 1 || K > 31 || (K % 2) == 0 || (C % 8) != 0) return DWB_ERR_BAD_SHAPE;
+  if (B == 0) return DWB_OK;
+  if (!x || !w || !y) return DWB_ERR_NULL_POINTER;
+  if (!aligned(x, 16) || !aligned(w, 16) || !aligned(y, 16)) return DWB_ERR_BAD_ALIGN;
+  if ((bias && !aligned(bias, 4)) || (scale && !aligned(scale, 4)) || (shift && !aligned(shift, 4)) ||
+      (residual && !aligned(residual, 4)))
+    return DWB_ERR_BAD_ALIGN;
+  return DWB_OK;
+}
+
+static dwb_problem make_problem(long long B, long long H, long long W, long long C, int K, int accum) {
+  dwb_problem pr;
+  pr.batch = B;
+  pr.height = H;
+  pr.width = W;
+  pr.channels = C;
+  pr.kernel_size = K;
+  pr.accum = accum;
+  return pr;
+}
+
+// Launch one plan (already checked against the problem).
+static int launch_plan(DeviceState* st, const dwb_plan& plan, const void* x, const void* w, const void* bias,
+                       const void* scale, const void* shift, const void* residual, void* y, long long B, long long H,
+                       long long W, long long C, int K, int act, void* stream) {
+  const KernelEntry* e = find_variant(K, plan.cols_per_thread, plan.rows_per_thread, plan.accum);
+  if (!e) return DWB_ERR_UNSUPPORTED;
+  int rc = ensure_smem_attr(st, e, plan.smem_bytes);
+  if (rc != DWB_OK) return rc;
+
+  CUtensorMap tmx, tmw;
+  rc = encode_x_map(&tmx, x, B, H, W, C, plan.tile_w_in);
+  if (rc != DWB_OK) return rc;
+  rc = encode_w_map(&tmw, w, C, K);
+  if (rc != DWB_OK) return rc;
+
+  DwParams p;
+  p.y = static_cast<__half*>(y);
+  p.bias = static_cast<const __half*>(bias);
+  p.scale = static_cast<const __half*>(scale);
+  p.shift = static_cast<const __half*>(shift);
+  p.residual = static_cast<const __half*>(residual);
+  p.B = static_cast<int>(B);
+  p.H = static_cast<int>(H);
+  p.W = static_cast<int>(W);
+  p.C = static_cast<int>(C);
+  p.tile_h = plan.tile_h;
+  p.tile_w = plan.tile_w;
+  p.tile_w_in = plan.tile_w_in;
+  p.tiles_h = static_cast<int>((H + plan.tile_h - 1) / plan.tile_h);
+  p.tiles_w = static_cast<int>((W + plan.tile_w - 1) / plan.tile_w);
+  p.cblocks = static_cast<int>((C + kChannelsPerCta - 1) / kChannelsPerCta);
+  p.ncg = plan.tile_w / plan.cols_per_thread;
+  p.consumer_warps = plan.consumer_warps;
+  p.ring_rows = plan.ring_rows;
+  p.ring_wrows = plan.ring_wrows;
+  p.act = act;
+  p.x_ring_off = kBarrierBytes;
+  p.w_ring_off = kBarrierBytes + static_cast<uint32_t>(plan.ring_rows) * plan.tile_w_in * kPixelBytes;
+  p.err = st->err_word;
+
+  void* args[3] = {&tmx, &tmw, &p};
+  const cudaError_t ce = cudaLaunchKernel(e->fn, dim3(static_cast<unsigned>(plan.grid)), dim3(plan.threads), args,
+                                          static_cast<size_t>(plan.smem_bytes), static_cast<cudaStream_t>(stream));
+  if (ce != cudaSuccess) {
+    (void)cudaGetLastError();
+    return cuda_fail("cudaLaunchKernel(dw_stream_kernel)", ce);
+  }
+  return DWB_OK;
+}
+
+// The planner's choice for a problem on this device, computed once.
+static int cached_plan(DeviceState* st, const dwb_problem& pr, dwb_plan* out) {
+  const PlanKey key{pr.batch, pr.height, pr.width, pr.channels, pr.kernel_size, pr.accum};
+  {
+    std::lock_guard<std::mutex> lk(st->plan_mu);
+    auto it = st->plans.find(key);
+    if (it != st->plans.end()) {
+      *out = it->second;
+      return DWB_OK;
+    }
+  }
+  const int rc = plan_problem(pr, st->hw, regs_of_variant, st, out);
+  if (rc != DWB_OK) return rc;
+  std::lock_guard<std::mutex> lk(st->plan_mu);
+  if (st->plans.size() > 4096) st->plans.clear();  // bound the cache
+  st->plans[key] = *out;
+  return DWB_OK;
+}
+
+// The single planner-driven launch path behind every entry point.
+static int launch_forward(const void* x, const void* w, const void* bias, const void* scale, const void* shift,
+                          const void* residual, void* y, long long B, long long H, long long W, long long C, int K,
+                          int act, int accum, void* stream) {
+  int rc = validate_args(x, w, bias, scale, shift, residual, y, B, H, W, C, K, act, accum);
+  if (rc != DWB_OK || B == 0) return rc;
+  DeviceState* st = nullptr;
+  rc = get_device_state(&st);
+  if (rc != DWB_OK) return rc;
+  dwb_plan plan;
+  rc = cached_plan(st, make_problem(B, H, W, C, K, accum), &plan);
+  if (rc != DWB_OK) return rc;
+  return launch_plan(st, plan, x, w, bias, scale, shift, residual, y, B, H, W, C, K, act, stream);
+}
+
+// Shared by the fixed-shape reference launchers.
+static int fixed_shape(int H, int W, int C, int K, int eH, int eW, int eC, int eK) {
+  return (H == eH && W == eW && C == eC && K == eK) ? DWB_OK : DWB_ERR_BAD_SHAPE;
+}
+
+}  // namespace dwb
+
+using namespace dwb;
+
+extern "C" {
+
+int dwb_abi_version(void) { return DWB_ABI_VERSION; }
+
+const char* dwb_status_string(int status) {
+  switch (status) {
+    case DWB_OK: return "ok";
+    case DWB_ERR_NULL_POINTER: return "a required pointer is NULL";
+    case DWB_ERR_BAD_SHAPE: return "shape outside the supported range or not the launcher's fixed shape";
+    case DWB_ERR_BAD_ALIGN: return "pointer not aligned (x, w, y need 16 bytes; bias/scale/shift/residual 4 bytes)";
+    case DWB_ERR_UNSUPPORTED: return "no compiled kernel variant fits this problem";
+    case DWB_ERR_CUDA: return "a CUDA runtime or driver call failed";
+    case DWB_ERR_NO_DEVICE: return "no usable sm_100 device is current";
+    case DWB_ERR_DEVICE_TIMEOUT: return "a kernel's bounded wait expired (device error word set)";
+    case DWB_ERR_BAD_ARG: return "an enum or flag argument is out of range";
+    default: return "unknown status";
+  }
+}
+
+int dwb_plan_query(const dwb_problem* problem, int sm_count, int smem_optin_bytes, dwb_plan* plan_out) {
+  if (!problem || !plan_out) return DWB_ERR_NULL_POINTER;
+  HwInfo hw;
+  if (sm_count > 0) hw.sm_count = sm_count;
+  if (smem_optin_bytes > 0) hw.smem_optin = smem_optin_bytes;
+  return plan_problem(*problem, hw, nullptr, nullptr, plan_out);
+}
+
+namespace {
+struct CandSink {
+  dwb_plan* out;
+  int cap;
+  int n;
+};
+void collect(const dwb_plan& p, void* vctx) {
+  CandSink* c = static_cast<CandSink*>(vctx);
+  if (c->n < c->cap) c->out[c->n] = p;
+  ++c->n;
+}
+}  // namespace
+
+int dwb_plan_candidates(const dwb_problem* problem, int sm_count, int smem_optin_bytes, dwb_plan* plans_out,
+                        int capacity, int* count_out) {
+  if (!problem || !count_out || (capacity > 0 && !plans_out)) return DWB_ERR_NULL_POINTER;
+  HwInfo hw;
+  if (sm_count > 0) hw.sm_count = sm_count;
+  if (smem_optin_bytes > 0) hw.smem_optin = smem_optin_bytes;
+  CandSink c{plans_out, capacity, 0};
+  const int rc = enumerate_plans(*problem, hw, nullptr, nullptr, collect, &c);
+  *count_out = c.n;
+  return rc;
+}
+
+const char* dwb_last_error(void) { return g_last_error; }
+
+int dwb_conv2d_nhwc_fwd_planned(const void* x, const void* w, const void* bias, const void* scale, const void* shift,
+                                const void* residual, void* y, int64_t B, int64_t H, int64_t W, int64_t C, int K,
+                                int act, const dwb_plan* plan, void* stream) {
+  if (!plan) return DWB_ERR_NULL_POINTER;
+  int rc = validate_args(x, w, bias, scale, shift, residual, y, B, H, W, C, K, act, plan->accum);
+  if (rc != DWB_OK || B == 0) return rc;
+  DeviceState* st = nullptr;
+  rc = get_device_state(&st);
+  if (rc != DWB_OK) return rc;
+  dwb_plan p = *plan;
+  const int regs = regs_of_variant(K, p.cols_per_thread, p.rows_per_thread, p.accum, st);
+  if (regs <= 0) return DWB_ERR_UNSUPPORTED;
+  rc = check_plan(make_problem(B, H, W, C, K, p.accum), st->hw, regs, &p);
+  if (rc != DWB_OK) return rc;
+  return launch_plan(st, p, x, w, bias, scale, shift, residual, y, B, H, W, C, K, act, stream);
+}
+
+int dwb_conv2d_nhwc_fwd(const void* x, const void* w, void* y, int64_t B, int64_t H, int64_t W, int64_t C, int K,
+                        void* stream) {
+  return launch_forward(x, w, nullptr, nullptr, nullptr, nullptr, y, B, H, W, C, K, DWB_ACT_NONE, DWB_ACCUM_F32,
+                        stream);
+}
+
+int dwb_conv2d_nhwc_fused_fwd(const void* x, const void* w, const void* bias, const void* scale, const void* shift,
+                              const void* residual, void* y, int64_t B, int64_t H, int64_t W, int64_t C, int K,
+                              int act, int accum, void* stream) {
+  return launch_forward(x, w, bias, scale, shift, residual, y, B, H, W, C, K, act, accum, stream);
+}
+
+int dwb_depthwise_forward_32_768_7(const void* input, const void* weight, void* output, int tensorHeight,
+                                   int tensorWidth, int Ch, int windowSize, int B, void* stream) {
+  int rc = fixed_shape(tensorHeight, tensorWidth, Ch, windowSize, 32, 32, 768, 7);
+  if (rc != DWB_OK) return rc;
+  return launch_forward(input, weight, nullptr, nullptr, nullptr, nullptr, output, B, 32, 32, 768, 7, DWB_ACT_NONE,
+                        DWB_ACCUM_F32, stream);
+}
+
+static int forward_32_1536_9(const void* input, const void* weight, void* output, int tensorHeight, int tensorWidth,
+                             int Ch, int windowSize, int B, int batchStride, void* stream) {
+  int rc = fixed_shape(tensorHeight, tensorWidth, Ch, windowSize, 32, 32, 1536, 9);
+  if (rc != DWB_OK) return rc;
+  if (batchStride != 32 * 32 * 1536) return DWB_ERR_BAD_SHAPE;  // images are packed NHWC
+  return launch_forward(input, weight, nullptr, nullptr, nullptr, nullptr, output, B, 32, 32, 1536, 9, DWB_ACT_NONE,
+                        DWB_ACCUM_F32, stream);
+}
+
+int dwb_depthwise_forward_32_1536_9(const void* input, const void* weight, void* output, int tensorHeight,
+                                    int tensorWidth, int Ch, int windowSize, int B, int batchStride, void* stream) {
+  return forward_32_1536_9(input, weight, output, tensorHeight, tensorWidth, Ch, windowSize, B, batchStride, stream);
+}
+
+int dwb_depthwise_forward_32_1536_9_v2(const void* input, const void* weight, void* output, int tensorHeight,
+                                       int tensorWidth, int Ch, int windowSize, int B, int batchStride,
+                                       void* stream) {
+  return forward_32_1536_9(input, weight, output, tensorHeight, tensorWidth, Ch, windowSize, B, batchStride, stream);
+}
+
+int dwb_depthwise_forward_16_1536_9(const void* input, const void* weight, void* output, int tensorHeight,
+                                    int tensorWidth, int Ch, int windowSize, int B, void* stream) {
+  int rc = fixed_shape(tensorHeight, tensorWidth, Ch, windowSize, 16, 16, 1536, 9);
+  if (rc != DWB_OK) return rc;
+  return launch_forward(input, weight, nullptr, nullptr, nullptr, nullptr, output, B, 16, 16, 1536, 9, DWB_ACT_NONE,
+                        DWB_ACCUM_F32, stream);
+}
+
+int dwb_depthwise_forward_32_1536_13(const void* input, const void* weight, void* output, int tensorHeight,
+                                     int tensorWidth, int Ch, int windowSize, int B, void* stream) {
+  int rc = fixed_shape(tensorHeight, tensorWidth, Ch, windowSize, 32, 32, 1536, 13);
+  if (rc != DWB_OK) return rc;
+  return launch_forward(input, weight, nullptr, nullptr, nullptr, nullptr, output, B, 32, 32, 1536, 13,
+                        DWB_ACT_NONE, DWB_ACCUM_F32, stream);
+}
+
+static int replknet_forward(const void* input, const void* weight, const void* bias, void* output, int B, int C,
+                            int H, int W, int eC, int eHW, int eK, void* stream) {
+  if (C != eC || H != eHW || W != eHW) return DWB_ERR_BAD_SHAPE;
+  return launch_forward(input, weight, bias, nullptr, nullptr, nullptr, output, B, H, W, C, eK, DWB_ACT_NONE,
+                        DWB_ACCUM_F32, stream);
+}
+
+int dwb_depthwise_31x31_128_nhwc(const void* input, const void* weight, const void* bias, void* output, int B, int C,
+                                 int H, int W, void* stream) {
+  return replknet_forward(input, weight, bias, output, B, C, H, W, 128, 56, 31, stream);
+}
+
+int dwb_depthwise_29x29_256_nhwc(const void* input, const void* weight, const void* bias, void* output, int B, int C,
+                                 int H, int W, void* stream) {
+  return replknet_forward(input, weight, bias, output, B, C, H, W, 256, 28, 29, stream);
+}
+
+int dwb_depthwise_27x27_512_nhwc(const void* input, const void* weight, const void* bias, void* output, int B, int C,
+                                 int H, int W, void* stream) {
+  return replknet_forward(input, weight, bias, output, B, C, H, W, 512, 14, 27, stream);
+}
+
+int dwb_device_error(int* code_out, int clear, void* stream) {
+  if (!code_out) return DWB_ERR_NULL_POINTER;
+  DeviceState* st = nullptr;
+  int rc = get_device_state(&st);
+  if (rc != DWB_OK) return rc;
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail("cudaStreamSynchronize", e);
+  int v = 0;
+  e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail("cudaMemcpyFromSymbol(g_device_error)", e);
+  if (clear) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+    if (e != cudaSuccess) return cuda_fail("cudaMemcpyToSymbol(g_device_error)", e);
+  }
+  *code_out = v;
+  return DWB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,213 @@
+// dw_planner.cpp -- choose (R, M, tile, rings) for the row-streaming kernel.
+//
+// The planner enumerates the compiled variants and tile shapes and keeps the
+// one with the lowest modelled time on the busiest SM:
+//   * work is counted in FMA-pipe clocks per warp: a valid (output row,
+//     kernel row) pair costs 2*R*K clocks of FFMA2 plus the conversion of the
+//     R + K - 1 staged inputs, and every kernel row costs the conversion of
+//     its K weights; rows whose input falls outside the image are not counted
+//     (the kernel skips them);
+//   * an SM runs min(ctas_per_sm, ...) CTAs at once over 4 sub-partitions;
+//     fewer than one resident warp per sub-partition idles the others;
+//   * every CTA streams (rows + weight rows) x 128-byte pixels from L2, at
+//     about 64 bytes per clock per SM.
+#include "dw_planner.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+namespace dwb {
+
+const int kVariantR[4] = {16, 14, 8, 7};
+const int kVariantM[2] = {2, 1};
+
+namespace {
+constexpr int kChannelsPerCta = 64;
+constexpr int kPixelBytes = 128;
+constexpr int kBarrierBytes = 1024;
+constexpr int kMaxConsumerWarps = 16;
+constexpr int kMaxBoxDim = 256;  // TMA box limit per dimension
+
+inline long long ceil_div(long long a, long long b) { return (a + b - 1) / b; }
+
+// Valid kernel rows for output row h (input rows inside [0, H)).
+inline int valid_taps(int h, int H, int K) {
+  const int pad = K / 2;
+  return std::min(K, H + pad - h) - std::max(0, pad - h);
+}
+}  // namespace
+
+int estimate_regs(int K, int R, int M, int acc) {
+  // accumulators (2 per output) + weights + addressing/temporaries
+  const int w = acc == 0 ? 2 * K : K;
+  const int part = acc == 0 ? 0 : R;
+  int est = 2 * M * R + (M == 1 ? w / 2 : w) + part + 24;
+  return std::min(255, std::max(40, est));
+}
+
+int validate_problem(const dwb_problem& pr) {
+  const long long B = pr.batch, H = pr.height, W = pr.width, C = pr.channels;
+  const int K = pr.kernel_size;
+  if (pr.accum != DWB_ACCUM_F32 && pr.accum != DWB_ACCUM_MIXED) return DWB_ERR_BAD_ARG;
+  if (B < 0 || H < 1 || W < 1 || C < 1) return DWB_ERR_BAD_SHAPE;
+  if (K < 1 || K > 31 || (K % 2) == 0) return DWB_ERR_BAD_SHAPE;
+  if (C % 8 != 0) return DWB_ERR_BAD_SHAPE;
+  if (H > (1LL << 30) || W > (1LL << 30) || C > (1LL << 30) || B > (1LL << 30)) return DWB_ERR_BAD_SHAPE;
+  return DWB_OK;
+}
+
+int enumerate_plans(const dwb_problem& pr, const HwInfo& hw, RegsFn regs, void* ctx, PlanSink sink, void* sink_ctx) {
+  const int vst = validate_problem(pr);
+  if (vst != DWB_OK) return vst;
+  const long long B = pr.batch, H = pr.height, W = pr.width, C = pr.channels;
+  const int K = pr.kernel_size;
+  const long long cblocks = ceil_div(C, kChannelsPerCta);
+  const int pad = K / 2;
+  int count = 0;
+
+  for (int ri = 0; ri < 4; ++ri) {
+    const int R = kVariantR[ri];
+    for (int mi = 0; mi < 2; ++mi) {
+      const int M = kVariantM[mi];
+      const int rg = regs ? regs(K, R, M, pr.accum, ctx) : estimate_regs(K, R, M, pr.accum);
+      if (rg <= 0) continue;  // variant not compiled
+      const int regs_alloc = ((rg + 7) / 8) * 8;
+      const int ncg_box = (kMaxBoxDim - (K - 1)) / R;
+      const int ncg_need = static_cast<int>(ceil_div(std::min<long long>(W, 8LL * R), R));
+      const int ncg_hi = std::min({8, ncg_box, ncg_need});
+      for (int ncg = 1; ncg <= ncg_hi; ++ncg) {
+        const int tile_w = ncg * R;
+        const int tile_w_in = tile_w + K - 1;
+        const long long tiles_w = ceil_div(W, tile_w);
+        for (int nrg = 1; nrg * ncg <= kMaxConsumerWarps; ++nrg) {
+          const int tile_h = nrg * M;
+          if (tile_h > H + M - 1) break;  // taller tiles only add empty rows
+          const int consumer_warps = nrg * ncg;
+          const int threads = (consumer_warps + 1) * 32;
+          if (static_cast<long long>(threads) * regs_alloc > hw.regs_per_sm) break;
+          const int ring_rows = std::min(tile_h + 2, tile_h + K - 1);
+          const int ring_wrows = std::min(3, K);
+          const long long smem = kBarrierBytes + static_cast<long long>(ring_rows) * tile_w_in * kPixelBytes +
+                                 static_cast<long long>(ring_wrows) * K * kPixelBytes;
+          if (smem > hw.smem_optin) break;
+          const int cps = static_cast<int>(std::min<long long>(
+              {hw.smem_per_sm / (smem + hw.smem_reserved), hw.regs_per_sm / (static_cast<long long>(threads) * regs_alloc),
+               hw.max_threads_sm / threads, hw.max_ctas_sm}));
+          if (cps < 1) continue;
+          const long long tiles_h = ceil_div(H, tile_h);
+          const long long grid = B * tiles_h * tiles_w * cblocks;
+          if (grid > 0x7fffffffLL) continue;
+
+          // Work per CTA, averaged over the tile rows of the image.
+          const double row_cost =
+              pr.accum == DWB_ACCUM_F32 ? 2.0 * R * K + 4.0 * (R + K - 1) : 2.0 * R * K + 6.0 * R;
+          const double wrow_cost = pr.accum == DWB_ACCUM_F32 ? 4.0 * K : 1.0 * K;
+          double work_sum = 0.0, bytes_sum = 0.0;
+          for (long long t = 0; t < tiles_h; ++t) {
+            const int h0 = static_cast<int>(t * tile_h);
+            const int rows_in = static_cast<int>(std::min<long long>(tile_h, H - h0));
+            const int s_lo = std::max(0, pad - (h0 + rows_in - 1));
+            const int s_hi = static_cast<int>(std::min<long long>(K, H + pad - h0));
+            const int nsteps = std::max(0, s_hi - s_lo);
+            double valid = 0.0;
+            for (int i = 0; i < rows_in; ++i) valid += valid_taps(h0 + i, static_cast<int>(H), K);
+            // per warp column group: every row group walks all steps
+            work_sum += ncg * (valid * row_cost + static_cast<double>(nsteps) * nrg * wrow_cost);
+            bytes_sum += (static_cast<double>(nsteps + tile_h - 1) * tile_w_in + nsteps * K) * kPixelBytes;
+          }
+          const double work_cta = work_sum / static_cast<double>(tiles_h);
+          const double bytes_cta = bytes_sum / static_cast<double>(tiles_h);
+          const long long ctas_busiest = ceil_div(grid, hw.sm_count);
+          const long long resident = std::min<long long>(cps, ctas_busiest);
+          const double warps_per_smsp = static_cast<double>(resident * consumer_warps) / 4.0;
+          const double util = warps_per_smsp >= 2.0 ? 1.0 : (warps_per_smsp >= 1.0 ? 0.85 : 0.85 * warps_per_smsp);
+          const double t_compute = static_cast<double>(ctas_busiest) * work_cta / (4.0 * util);
+          const double t_load = static_cast<double>(ctas_busiest) * bytes_cta / 64.0;
+          const double waves = std::ceil(static_cast<double>(ctas_busiest) / static_cast<double>(cps));
+          const double cost = std::max(t_compute, t_load) + waves * 2000.0;
+          dwb_plan pl;
+          std::memset(&pl, 0, sizeof(pl));
+          pl.kernel_size = K;
+          pl.cols_per_thread = R;
+          pl.rows_per_thread = M;
+          pl.channel_block = kChannelsPerCta;
+          pl.tile_h = tile_h;
+          pl.tile_w = tile_w;
+          pl.tile_w_in = tile_w_in;
+          pl.ring_rows = ring_rows;
+          pl.ring_wrows = ring_wrows;
+          pl.consumer_warps = consumer_warps;
+          pl.threads = threads;
+          pl.smem_bytes = static_cast<int32_t>(smem);
+          pl.ctas_per_sm = cps;
+          pl.grid = grid;
+          pl.accum = pr.accum;
+          pl.regs_estimate = rg;
+          pl.model_cost = cost;
+          ++count;
+          if (sink) sink(pl, sink_ctx);
+        }
+      }
+    }
+  }
+  return count > 0 ? DWB_OK : DWB_ERR_UNSUPPORTED;
+}
+
+namespace {
+struct BestSink {
+  dwb_plan best;
+  bool found = false;
+};
+void keep_best(const dwb_plan& p, void* vctx) {
+  BestSink* b = static_cast<BestSink*>(vctx);
+  if (!b->found || p.model_cost < b->best.model_cost * 0.999) {
+    b->best = p;
+    b->found = true;
+  }
+}
+}  // namespace
+
+int plan_problem(const dwb_problem& pr, const HwInfo& hw, RegsFn regs, void* ctx, dwb_plan* out) {
+  if (!out) return DWB_ERR_NULL_POINTER;
+  std::memset(out, 0, sizeof(*out));
+  BestSink b;
+  const int rc = enumerate_plans(pr, hw, regs, ctx, keep_best, &b);
+  if (rc != DWB_OK) return rc;
+  if (!b.found) return DWB_ERR_UNSUPPORTED;
+  *out = b.best;
+  return DWB_OK;
+}
+
+// Recompute every derived field of a caller-supplied plan and check it
+// against the kernel's requirements.
+int check_plan(const dwb_problem& pr, const HwInfo& hw, int regs, dwb_plan* p) {
+  const int vst = validate_problem(pr);
+  if (vst != DWB_OK) return vst;
+  const int K = pr.kernel_size;
+  const int R = p->cols_per_thread, M = p->rows_per_thread;
+  bool known_r = false;
+  for (int r : kVariantR) known_r |= (r == R);
+  if (!known_r || (M != 1 && M != 2) || p->kernel_size != K || p->accum != pr.accum) return DWB_ERR_BAD_ARG;
+  if (p->tile_w < R || p->tile_w % R != 0 || p->tile_h < M || p->tile_h % M != 0) return DWB_ERR_BAD_ARG;
+  if (p->tile_w + K - 1 > kMaxBoxDim) return DWB_ERR_BAD_ARG;
+  const int cw = (p->tile_w / R) * (p->tile_h / M);
+  if (cw < 1 || cw > 31) return DWB_ERR_BAD_ARG;
+  if (p->ring_rows < p->tile_h || p->ring_rows > 60 || p->ring_wrows < 1 || p->ring_wrows > K) return DWB_ERR_BAD_ARG;
+  p->channel_block = kChannelsPerCta;
+  p->tile_w_in = p->tile_w + K - 1;
+  p->consumer_warps = cw;
+  p->threads = 32 * (cw + 1);
+  const long long smem = kBarrierBytes + static_cast<long long>(p->ring_rows) * p->tile_w_in * kPixelBytes +
+                         static_cast<long long>(p->ring_wrows) * K * kPixelBytes;
+  if (smem > hw.smem_optin) return DWB_ERR_BAD_ARG;
+  if (regs > 0 && static_cast<long long>(p->threads) * ((regs + 7) / 8 * 8) > hw.regs_per_sm) return DWB_ERR_BAD_ARG;
+  p->smem_bytes = static_cast<int32_t>(smem);
+  p->grid = pr.batch * ceil_div(pr.height, p->tile_h) * ceil_div(pr.width, p->tile_w) *
+            ceil_div(pr.channels, kChannelsPerCta);
+  if (p->grid > 0x7fffffffLL) return DWB_ERR_BAD_SHAPE;
+  p->regs_estimate = regs;
+  return DWB_OK;
+}
+
+}  // namespace dwb

@@ -1,0 +1,49 @@
+// dw_planner.h -- launch/tiling planner for the row-streaming depthwise kernel.
+//
+// Pure host arithmetic (no CUDA calls), so it is exercised on machines
+// without a GPU through dwb_plan_query().  The launcher calls the same
+// function with the real per-variant register counts of the loaded device.
+#pragma once
+
+#include <stdint.h>
+
+#include "../../include/dwconv_b200.h"
+
+namespace dwb {
+
+struct HwInfo {
+  int sm_count = 148;          // B200
+  int smem_optin = 232448;     // max dynamic smem per CTA (227 KB)
+  int smem_per_sm = 233472;    // 228 KB per SM
+  int smem_reserved = 1024;    // per-CTA system reservation
+  int regs_per_sm = 65536;
+  int max_threads_sm = 2048;
+  int max_ctas_sm = 32;
+};
+
+// Register count of a compiled variant, or 0 when the variant is not built.
+typedef int (*RegsFn)(int K, int R, int M, int acc, void* ctx);
+
+// Register estimate used when no device is present (matches ptxas within a
+// few registers for the variants in dw_variants.cuh).
+int estimate_regs(int K, int R, int M, int acc);
+
+// Column-group sizes and row blockings the library compiles (dw_variants.cuh).
+extern const int kVariantR[4];
+extern const int kVariantM[2];
+
+// Range checks shared by every entry point.  Returns a dwb_status.
+int validate_problem(const dwb_problem& pr);
+
+// Call `sink` for every feasible plan (with its modelled cost).
+typedef void (*PlanSink)(const dwb_plan& plan, void* ctx);
+int enumerate_plans(const dwb_problem& pr, const HwInfo& hw, RegsFn regs, void* ctx, PlanSink sink, void* sink_ctx);
+
+// Validate the problem and fill *out with the lowest-cost plan.
+int plan_problem(const dwb_problem& pr, const HwInfo& hw, RegsFn regs, void* ctx, dwb_plan* out);
+
+// Check a caller-supplied plan (R, M, tile_h, tile_w, ring sizes, accum) and
+// recompute its derived fields.  regs: the variant's registers (0 = unknown).
+int check_plan(const dwb_problem& pr, const HwInfo& hw, int regs, dwb_plan* p);
+
+}  // namespace dwb

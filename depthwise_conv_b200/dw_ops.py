@@ -1,0 +1,152 @@
+"""Tensor-level entry points of the engine and the generic torch ops.
+
+Everything here validates tensors, allocates the output with the torch
+caching allocator and calls the C ABI on ``torch.cuda.current_stream()``;
+the arithmetic happens only in ``libdwconv_b200.so``.  There is no CPU or
+PyTorch fallback: a CPU tensor, a wrong dtype or layout raises RuntimeError.
+
+Generic ops (new; the reference only has fixed-shape ops):
+
+* ``depthwise::conv2d_nhwc(Tensor input, Tensor weight, Tensor? bias=None) -> Tensor``
+* ``depthwise::conv2d_nhwc_fused(Tensor input, Tensor weight, Tensor? bias, Tensor? scale,
+  Tensor? shift, Tensor? residual, int act) -> Tensor`` computing
+  ``act(conv + bias) * scale + shift + residual`` in one kernel -- the
+  semantics of the reference's fused baseline
+  (benchmark_cudnn_fused_e2e.py:44-84,115-134) plus ConvMixer's residual
+  (convmixer/convmixer.py:58-59).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+ACT_CODES = _lib.ACT_CODES
+
+
+def _stream_of(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def check_input(x: torch.Tensor, name: str = "input") -> None:
+    if not x.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor (the engine has no CPU path)")
+    if x.dtype != torch.float16:
+        raise RuntimeError(f"{name} must be float16, got {x.dtype}")
+    if x.dim() != 4:
+        raise RuntimeError(f"{name} must be 4-D [B, C, H, W], got {tuple(x.shape)}")
+    if not x.is_contiguous(memory_format=torch.channels_last):
+        raise RuntimeError(f"{name} must be channels_last")
+
+
+def check_weight(w: torch.Tensor, C: int) -> int:
+    if not w.is_cuda or w.dtype != torch.float16:
+        raise RuntimeError("weight must be a float16 CUDA tensor")
+    if w.dim() != 3 or w.shape[0] != w.shape[1] or w.shape[2] != C or not w.is_contiguous():
+        raise RuntimeError(f"weight must be contiguous [K, K, C={C}], got {tuple(w.shape)}")
+    return int(w.shape[0])
+
+
+def check_vec(v, C: int, name: str, device) -> int:
+    if v is None or v.numel() == 0:
+        return 0
+    if not v.is_cuda or v.dtype != torch.float16 or v.numel() != C or not v.is_contiguous():
+        raise RuntimeError(f"{name} must be a contiguous float16 CUDA tensor with {C} elements")
+    if v.device != device:
+        raise RuntimeError(f"{name} is on {v.device}, input on {device}")
+    return v.data_ptr()
+
+
+class _DeviceGuard:
+    """Make the tensor's device current for the C ABI (cheap when it already is)."""
+
+    def __init__(self, device: torch.device):
+        self.idx = device.index
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self.idx:
+            self.prev = cur
+            torch.cuda.set_device(self.idx)
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+
+
+def conv2d_nhwc_fused(x: torch.Tensor, w: torch.Tensor, bias=None, scale=None, shift=None, residual=None,
+                      act: int | str = 0, accum: int = _lib.ACCUM_F32, out: torch.Tensor | None = None,
+                      plan: dict | None = None):
+    """y = act(conv(x, w) + bias) * scale + shift + residual (each term optional).
+
+    x: channels_last [B, C, H, W] fp16; w: [K, K, C] fp16.  Returns y like x.
+    ``plan``: an explicit launch plan (a dict from ``plan_candidates``) instead
+    of the planner's choice -- for autotuning.
+    """
+    check_input(x)
+    B, C, H, W = x.shape
+    K = check_weight(w, C)
+    if w.device != x.device:
+        raise RuntimeError(f"weight is on {w.device}, input on {x.device}")
+    act_code = ACT_CODES[act] if isinstance(act, str) else int(act)
+    bp = check_vec(bias, C, "bias", x.device)
+    sp = check_vec(scale, C, "scale", x.device)
+    hp = check_vec(shift, C, "shift", x.device)
+    rp = 0
+    if residual is not None:
+        check_input(residual, "residual")
+        if residual.shape != x.shape or residual.device != x.device:
+            raise RuntimeError("residual must match input in shape and device")
+        rp = residual.data_ptr()
+    y = torch.empty_like(x, memory_format=torch.channels_last) if out is None else out
+    if out is not None:
+        check_input(out, "out")
+        if out.shape != x.shape:
+            raise RuntimeError("out must match input in shape")
+    with _DeviceGuard(x.device):
+        if plan is None:
+            _lib.call("dwb_conv2d_nhwc_fused_fwd", x.data_ptr(), w.data_ptr(), bp or None, sp or None, hp or None,
+                      rp or None, y.data_ptr(), B, H, W, C, K, act_code, int(accum), _stream_of(x))
+        else:
+            pl = _lib.Plan.from_dict(plan)
+            _lib.call("dwb_conv2d_nhwc_fwd_planned", x.data_ptr(), w.data_ptr(), bp or None, sp or None,
+                      hp or None, rp or None, y.data_ptr(), B, H, W, C, K, act_code, ctypes.byref(pl),
+                      _stream_of(x))
+    return y
+
+
+def conv2d_nhwc(x: torch.Tensor, w: torch.Tensor, bias=None) -> torch.Tensor:
+    """y = conv(x, w) (+ bias): the plain depthwise convolution."""
+    return conv2d_nhwc_fused(x, w, bias=bias)
+
+
+# ---- generic torch.library ops ---------------------------------------------------
+
+torch.library.define("depthwise::conv2d_nhwc", "(Tensor input, Tensor weight, Tensor? bias=None) -> Tensor")
+torch.library.define(
+    "depthwise::conv2d_nhwc_fused",
+    "(Tensor input, Tensor weight, Tensor? bias, Tensor? scale, Tensor? shift, Tensor? residual, int act) -> Tensor",
+)
+
+
+@torch.library.impl("depthwise::conv2d_nhwc", "default")
+def _conv2d_nhwc_impl(input, weight, bias=None):
+    return conv2d_nhwc_fused(input, weight, bias=bias)
+
+
+@torch.library.impl("depthwise::conv2d_nhwc_fused", "default")
+def _conv2d_nhwc_fused_impl(input, weight, bias, scale, shift, residual, act):
+    return conv2d_nhwc_fused(input, weight, bias, scale, shift, residual, act)
+
+
+@torch.library.register_fake("depthwise::conv2d_nhwc")
+def _conv2d_nhwc_fake(input, weight, bias=None):
+    return torch.empty_like(input)
+
+
+@torch.library.register_fake("depthwise::conv2d_nhwc_fused")
+def _conv2d_nhwc_fused_fake(input, weight, bias, scale, shift, residual, act):
+    return torch.empty_like(input)

@@ -1,0 +1,204 @@
+/*
+ * dwconv_b200.h -- C ABI of the B200 (sm_100a) depthwise-convolution engine.
+ *
+ * Scope: the FP16 NHWC forward depthwise convolution, stride 1, "same"
+ * padding (pad = K/2 on every side), odd kernel sizes 1..31, with an optional
+ * fused epilogue  y = act(conv(x) + bias) * scale + shift (+ residual).
+ *
+ * Conventions shared by every entry point:
+ *   - All tensor pointers are DEVICE pointers to IEEE binary16 data.
+ *   - x, y, residual: NHWC, i.e. the physical layout of a channels_last
+ *     [B, C, H, W] tensor; element (b, h, w, c) at ((b*H + h)*W + w)*C + c.
+ *   - w: [K][K][C] contiguous (tap-major, channel innermost), the layout the
+ *     reference's torch ops take (convmixer/kernels/depthwise_torch_ops.py:202-205,
+ *     replknet/kernels/depthwise_replknet_nhwc_ops.py:113).
+ *   - bias, scale, shift: [C] or NULL (NULL means 0 / 1 / 0 respectively).
+ *   - stream: a cudaStream_t passed as void*; NULL is the legacy default
+ *     stream.  Every launch goes on this stream only, and no entry point
+ *     synchronises, allocates device memory or calls back into the host, so
+ *     all of them can be captured into CUDA graphs.
+ *   - Return value: a dwb_status code.  Errors are reported, never exit().
+ *   - Requirements: C % 8 == 0 (16-byte channel rows for TMA), x / w / y
+ *     16-byte aligned, 1 <= K <= 31 and K odd, B,H,W >= 1 (B == 0 is a no-op).
+ *
+ * The engine allocates nothing: the caller owns every buffer.
+ */
+#ifndef DWCONV_B200_H
+#define DWCONV_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DWB_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define DWB_API __attribute__((visibility("default")))
+#else
+#define DWB_API
+#endif
+
+typedef enum dwb_status {
+    DWB_OK = 0,
+    DWB_ERR_NULL_POINTER = 1,   /* a required pointer is NULL                    */
+    DWB_ERR_BAD_SHAPE = 2,      /* shape outside the supported range / mismatch  */
+    DWB_ERR_BAD_ALIGN = 3,      /* pointer not 16-byte aligned                   */
+    DWB_ERR_UNSUPPORTED = 4,    /* valid request this build has no kernel for    */
+    DWB_ERR_CUDA = 5,           /* a CUDA runtime / driver call failed           */
+    DWB_ERR_NO_DEVICE = 6,      /* no usable sm_100 device                       */
+    DWB_ERR_DEVICE_TIMEOUT = 7, /* a kernel's bounded wait expired (device flag) */
+    DWB_ERR_BAD_ARG = 8         /* an enum / flag argument is out of range       */
+} dwb_status;
+
+typedef enum dwb_act {
+    DWB_ACT_NONE = 0,
+    DWB_ACT_RELU = 1,
+    DWB_ACT_GELU = 2            /* exact erf GELU, as nn.GELU() default          */
+} dwb_act;
+
+typedef enum dwb_accum {
+    DWB_ACCUM_F32 = 0,          /* fp32 accumulation of every tap (default)      */
+    DWB_ACCUM_MIXED = 1         /* fp16x2 per kernel row, fp32 across rows       */
+} dwb_accum;
+
+/* Problem description used by the planner. */
+typedef struct dwb_problem {
+    int64_t batch, height, width, channels;
+    int32_t kernel_size;
+    int32_t accum;              /* dwb_accum */
+} dwb_problem;
+
+/* Launch plan chosen by the planner (all fields are outputs). */
+typedef struct dwb_plan {
+    int32_t kernel_size;
+    int32_t cols_per_thread;    /* R: output columns a thread owns              */
+    int32_t rows_per_thread;    /* M: output rows a thread owns                 */
+    int32_t channel_block;      /* CB: channels per CTA (2 per lane)            */
+    int32_t tile_h, tile_w;     /* output tile per CTA                          */
+    int32_t tile_w_in;          /* input columns staged per row (tile_w + K-1)  */
+    int32_t ring_rows;          /* input-row ring slots                         */
+    int32_t ring_wrows;         /* weight-row ring slots                        */
+    int32_t consumer_warps;
+    int32_t threads;
+    int32_t smem_bytes;
+    int32_t ctas_per_sm;
+    int64_t grid;               /* CTAs launched                                */
+    int32_t accum;              /* dwb_accum actually used                      */
+    int32_t regs_estimate;      /* registers/thread assumed by the planner      */
+    double model_cost;          /* planner's modelled time (arbitrary units)     */
+} dwb_plan;
+
+/* ---- library information ------------------------------------------------ */
+
+DWB_API int dwb_abi_version(void);
+DWB_API const char* dwb_status_string(int status);
+
+/* Plan a problem without touching the GPU (pure host arithmetic).
+ * sm_count / smem_optin_bytes describe the target (148 / 232448 on B200);
+ * pass 0 for both to use the B200 defaults. */
+DWB_API int dwb_plan_query(const dwb_problem* problem, int sm_count, int smem_optin_bytes,
+                   dwb_plan* plan_out);
+
+/* Every feasible plan for a problem (host arithmetic only), in the planner's
+ * enumeration order, for autotuning.  Writes at most `capacity` plans and
+ * the total number of feasible plans to *count_out. */
+DWB_API int dwb_plan_candidates(const dwb_problem* problem, int sm_count, int smem_optin_bytes,
+                                dwb_plan* plans_out, int capacity, int* count_out);
+
+/* Text of the last CUDA runtime/driver failure seen by the calling thread
+ * (behind a DWB_ERR_CUDA status), or "" if none. */
+DWB_API const char* dwb_last_error(void);
+
+/* ---- generic entry points ------------------------------------------------ */
+
+/* y = conv(x, w): the plain depthwise convolution (no bias). */
+DWB_API int dwb_conv2d_nhwc_fwd(const void* x, const void* w, void* y,
+                        int64_t B, int64_t H, int64_t W, int64_t C, int K,
+                        void* stream);
+
+/* y = act(conv(x, w) + bias) * scale + shift (+ residual), in one kernel.
+ * Any of bias / scale / shift / residual may be NULL.  accum: dwb_accum. */
+DWB_API int dwb_conv2d_nhwc_fused_fwd(const void* x, const void* w, const void* bias,
+                              const void* scale, const void* shift,
+                              const void* residual, void* y,
+                              int64_t B, int64_t H, int64_t W, int64_t C, int K,
+                              int act, int accum, void* stream);
+
+/* As dwb_conv2d_nhwc_fused_fwd, with a caller-chosen plan instead of the
+ * planner's (for autotuning).  The plan's cols_per_thread, rows_per_thread,
+ * tile_h, tile_w, ring_rows, ring_wrows and accum are used; every derived
+ * field is recomputed, and an inconsistent plan returns DWB_ERR_BAD_ARG. */
+DWB_API int dwb_conv2d_nhwc_fwd_planned(const void* x, const void* w, const void* bias,
+                                        const void* scale, const void* shift,
+                                        const void* residual, void* y,
+                                        int64_t B, int64_t H, int64_t W, int64_t C, int K,
+                                        int act, const dwb_plan* plan, void* stream);
+
+/* ---- reference-facing entry points --------------------------------------
+ * One per launcher of luckychen/depthwise_conv on this path, with the same
+ * argument meaning.  Where the reference loops over the batch in Python
+ * (depthwise_torch_ops.py:113,122,131) the batch B is passed here instead and
+ * all images run in one launch.  A shape that does not match the launcher's
+ * fixed (H, W, C, K) returns DWB_ERR_BAD_SHAPE where the reference prints and
+ * calls exit(1). */
+
+/* replaces depthwise_forward_32_768_7, convmixer/kernels/depthwise_integration.cu:114-133 */
+DWB_API int dwb_depthwise_forward_32_768_7(const void* input, const void* weight, void* output,
+                                   int tensorHeight, int tensorWidth, int Ch,
+                                   int windowSize, int B, void* stream);
+
+/* replaces depthwise_forward_32_1536_9, convmixer/kernels/depthwise_integration.cu:398-421 */
+DWB_API int dwb_depthwise_forward_32_1536_9(const void* input, const void* weight, void* output,
+                                    int tensorHeight, int tensorWidth, int Ch,
+                                    int windowSize, int B, int batchStride,
+                                    void* stream);
+
+/* replaces depthwise_forward_32_1536_9_v2, convmixer/kernels/depthwise_integration.cu:707-730 */
+DWB_API int dwb_depthwise_forward_32_1536_9_v2(const void* input, const void* weight, void* output,
+                                       int tensorHeight, int tensorWidth, int Ch,
+                                       int windowSize, int B, int batchStride,
+                                       void* stream);
+
+/* replaces depthwise_forward_16_1536_9, convmixer/kernels/depthwise_integration.cu:984-1003 */
+DWB_API int dwb_depthwise_forward_16_1536_9(const void* input, const void* weight, void* output,
+                                    int tensorHeight, int tensorWidth, int Ch,
+                                    int windowSize, int B, void* stream);
+
+/* replaces depthwise_forward_32_1536_13, convmixer/kernels/depthwise_integration.cu:1013-1030
+ * (a stub that exits in the reference; implemented here) */
+DWB_API int dwb_depthwise_forward_32_1536_13(const void* input, const void* weight, void* output,
+                                     int tensorHeight, int tensorWidth, int Ch,
+                                     int windowSize, int B, void* stream);
+
+/* replaces depthwise_31x31_128_nhwc, replknet/kernels/depthwise_replknet_nhwc_integration.cu:60-98
+ * bias may be NULL (the reference's empty-tensor case, :73); the bias add is
+ * fused instead of the reference's separate bias_add_nhwc_kernel (:23-28). */
+DWB_API int dwb_depthwise_31x31_128_nhwc(const void* input, const void* weight, const void* bias,
+                                 void* output, int B, int C, int H, int W, void* stream);
+
+/* replaces depthwise_29x29_256_nhwc, replknet/kernels/depthwise_replknet_nhwc_integration.cu:103-141 */
+DWB_API int dwb_depthwise_29x29_256_nhwc(const void* input, const void* weight, const void* bias,
+                                 void* output, int B, int C, int H, int W, void* stream);
+
+/* replaces depthwise_27x27_512_nhwc, replknet/kernels/depthwise_replknet_nhwc_integration.cu:146-184 */
+DWB_API int dwb_depthwise_27x27_512_nhwc(const void* input, const void* weight, const void* bias,
+                                 void* output, int B, int C, int H, int W, void* stream);
+
+/* ---- diagnostics ----------------------------------------------------------- */
+
+/* Read (and optionally clear) the device-side error word of the current
+ * device: 0 = no error, otherwise a code set by a kernel whose bounded
+ * mbarrier wait expired.  Synchronises the given stream first. */
+DWB_API int dwb_device_error(int* code_out, int clear, void* stream);
+
+/* Measure the CUDA-core FMA rate of the current device with a short
+ * microbenchmark (fp16x2 HFMA2 and fp32x2 FFMA2), in TFLOP/s. */
+DWB_API int dwb_probe_fma_peak(double* hfma2_tflops, double* ffma2_tflops, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DWCONV_B200_H */

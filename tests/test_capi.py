@@ -1,0 +1,118 @@
+"""The C-ABI library on a machine without a GPU: it loads, exports every
+declared symbol, validates arguments before touching a device, and plans
+every benchmark configuration within the hardware limits."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "dwconv_b200.h")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from depthwise_conv_b200 import _lib
+    return _lib.load()
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"DWB_API\s+[\w\s\*]+?\b(dwb_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_abi():
+    syms = declared_symbols()
+    assert "dwb_conv2d_nhwc_fused_fwd" in syms and "dwb_depthwise_31x31_128_nhwc" in syms
+    assert len(syms) >= 15
+
+
+def test_every_declared_symbol_is_exported_and_bound(lib):
+    from depthwise_conv_b200 import _lib
+    for s in declared_symbols():
+        assert hasattr(lib, s), f"{s} not exported by libdwconv_b200.so"
+        assert s in _lib.SIGNATURES, f"{s} has no ctypes binding"
+
+
+def test_abi_version_and_status_strings(lib):
+    from depthwise_conv_b200 import _lib
+    assert lib.dwb_abi_version() == 1
+    for code in range(9):
+        assert lib.dwb_status_string(code) and b"unknown" not in lib.dwb_status_string(code)
+    assert lib.dwb_status_string(99) == b"unknown status"
+    assert _lib.status_string(_lib.ERR_BAD_SHAPE).startswith("shape")
+
+
+# Fake (never dereferenced) but 16-byte aligned addresses: every call below is
+# rejected by argument validation before any CUDA call.
+X, Wt, Y = 0x10000, 0x20000, 0x30000
+
+
+def test_validation_statuses(lib):
+    from depthwise_conv_b200 import _lib as L
+    f = lib.dwb_conv2d_nhwc_fwd
+    assert f(None, Wt, Y, 1, 8, 8, 64, 7, None) == L.ERR_NULL_POINTER
+    assert f(X, None, Y, 1, 8, 8, 64, 7, None) == L.ERR_NULL_POINTER
+    assert f(X, Wt, Y, 1, 8, 8, 64, 8, None) == L.ERR_BAD_SHAPE       # even K
+    assert f(X, Wt, Y, 1, 8, 8, 64, 33, None) == L.ERR_BAD_SHAPE      # K > 31
+    assert f(X, Wt, Y, 1, 8, 8, 60, 7, None) == L.ERR_BAD_SHAPE       # C % 8
+    assert f(X, Wt, Y, 1, 0, 8, 64, 7, None) == L.ERR_BAD_SHAPE       # H = 0
+    assert f(X + 2, Wt, Y, 1, 8, 8, 64, 7, None) == L.ERR_BAD_ALIGN
+    assert f(X, Wt, Y + 8, 1, 8, 8, 64, 7, None) == L.ERR_BAD_ALIGN
+    assert f(X, Wt, Y, 0, 8, 8, 64, 7, None) == L.OK                  # empty batch: no-op
+    g = lib.dwb_conv2d_nhwc_fused_fwd
+    assert g(X, Wt, None, None, None, None, Y, 1, 8, 8, 64, 7, 3, 0, None) == L.ERR_BAD_ARG   # act
+    assert g(X, Wt, None, None, None, None, Y, 1, 8, 8, 64, 7, 0, 2, None) == L.ERR_BAD_ARG   # accum
+    assert g(X, Wt, 0x40001, None, None, None, Y, 1, 8, 8, 64, 7, 0, 0, None) == L.ERR_BAD_ALIGN
+
+
+def test_fixed_shape_launchers_reject_other_shapes(lib):
+    from depthwise_conv_b200 import _lib as L
+    assert lib.dwb_depthwise_forward_32_768_7(X, Wt, Y, 16, 32, 768, 7, 1, None) == L.ERR_BAD_SHAPE
+    assert lib.dwb_depthwise_forward_32_1536_9(X, Wt, Y, 32, 32, 1536, 7, 1, 32 * 32 * 1536, None) == L.ERR_BAD_SHAPE
+    assert lib.dwb_depthwise_forward_32_1536_9(X, Wt, Y, 32, 32, 1536, 9, 1, 12345, None) == L.ERR_BAD_SHAPE
+    assert lib.dwb_depthwise_forward_32_1536_9_v2(X, Wt, Y, 32, 31, 1536, 9, 1, 0, None) == L.ERR_BAD_SHAPE
+    assert lib.dwb_depthwise_forward_16_1536_9(X, Wt, Y, 16, 16, 1024, 9, 1, None) == L.ERR_BAD_SHAPE
+    assert lib.dwb_depthwise_forward_32_1536_13(X, Wt, Y, 32, 32, 1536, 11, 1, None) == L.ERR_BAD_SHAPE
+    assert lib.dwb_depthwise_31x31_128_nhwc(X, Wt, None, Y, 1, 128, 56, 55, None) == L.ERR_BAD_SHAPE
+    assert lib.dwb_depthwise_29x29_256_nhwc(X, Wt, None, Y, 1, 128, 28, 28, None) == L.ERR_BAD_SHAPE
+    assert lib.dwb_depthwise_27x27_512_nhwc(X, Wt, None, Y, 1, 512, 15, 14, None) == L.ERR_BAD_SHAPE
+    # right shape, zero batch: accepted without a device
+    assert lib.dwb_depthwise_31x31_128_nhwc(X, Wt, None, Y, 0, 128, 56, 56, None) == L.OK
+
+
+BASELINE_SHAPES = [
+    (1, 32, 32, 768, 7), (1, 32, 32, 1536, 9), (1, 56, 56, 128, 31), (1, 28, 28, 256, 29), (1, 14, 14, 512, 27),
+    (1, 7, 7, 1024, 13), (16, 32, 32, 1536, 9), (64, 32, 32, 1536, 9), (256, 32, 32, 1536, 9),
+    (1, 16, 16, 1536, 9), (1, 32, 32, 1536, 13),
+] + [(64, 56, 56, 1024, k) for k in (7, 9, 13, 17, 21, 27, 29, 31)]
+
+
+@pytest.mark.parametrize("B,H,W,C,K", BASELINE_SHAPES + [(2, 23, 17, 72, 5), (1, 1, 1, 8, 1), (3, 300, 500, 16, 31)])
+@pytest.mark.parametrize("accum", [0, 1])
+def test_plans_respect_hardware_limits(B, H, W, C, K, accum):
+    from depthwise_conv_b200 import _lib
+    p = _lib.plan_query(B, H, W, C, K, accum)
+    assert p["kernel_size"] == K and p["accum"] == accum
+    R, M = p["cols_per_thread"], p["rows_per_thread"]
+    assert R in (7, 8, 14, 16) and M in (1, 2)
+    assert p["tile_w"] % R == 0 and p["tile_h"] % M == 0
+    assert p["tile_w_in"] == p["tile_w"] + K - 1 <= 256                 # TMA box limit
+    assert p["consumer_warps"] == (p["tile_w"] // R) * (p["tile_h"] // M)
+    assert p["threads"] == 32 * (p["consumer_warps"] + 1) <= 1024
+    assert p["threads"] * ((p["regs_estimate"] + 7) // 8 * 8) <= 65536
+    assert p["smem_bytes"] <= 232448 and p["ctas_per_sm"] >= 1
+    assert p["ring_rows"] >= p["tile_h"] and p["ring_wrows"] >= 1
+    tiles = -(-H // p["tile_h"]) * -(-W // p["tile_w"]) * -(-C // 64)
+    assert p["grid"] == B * tiles
+
+
+def test_plan_rejects_bad_problems():
+    from depthwise_conv_b200 import _lib
+    with pytest.raises(_lib.DwbError):
+        _lib.plan_query(1, 8, 8, 64, 6)
+    with pytest.raises(_lib.DwbError):
+        _lib.plan_query(1, 8, 8, 12, 7)

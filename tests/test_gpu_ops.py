@@ -1,0 +1,205 @@
+"""The reference-facing torch ops and the C ABI on the GPU.
+
+Mirrors how the reference's scripts exercise the path: the fixed-shape ops
+(depthwise_torch_ops.py:93-133, depthwise_replknet_nhwc_ops.py:71-86), the
+nn.Module swappers, torch.compile in default and reduce-overhead modes, and
+the CUDA-graph replay check of verify_e5b_correctness.py:26-37.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+import torch.nn as nn
+
+from conftest import make_problem
+
+pytestmark = pytest.mark.gpu
+
+MAX_TOL, REL_TOL = 1e-2, 1e-3
+
+
+@pytest.fixture(scope="module")
+def eng():
+    import depthwise_conv_b200 as d
+    return d
+
+
+def to_dev(a):
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    return t.permute(0, 3, 1, 2) if t.dim() == 4 else t
+
+
+def to_host(t):
+    return t.permute(0, 2, 3, 1).contiguous().cpu().numpy()
+
+
+def check(O, y, exact, what=""):
+    max_err, rel = O.parity(to_host(y).astype(np.float64), exact)
+    assert max_err <= MAX_TOL and rel <= REL_TOL, f"{what}: max {max_err:.3e} rel {rel:.3e}"
+
+
+FIXED = [("conv2d_32_768_7", 32, 768, 7), ("conv2d_32_1536_9", 32, 1536, 9), ("conv2d_32_1536_9_v2", 32, 1536, 9),
+         ("conv2d_16_1536_9", 16, 1536, 9), ("conv2d_32_1536_13", 32, 1536, 13)]
+
+
+@pytest.mark.parametrize("op,HW,C,K", FIXED, ids=[f[0] for f in FIXED])
+@pytest.mark.parametrize("B", [1, 3])
+def test_convmixer_ops(eng, oracle_mod, op, HW, C, K, B):
+    x, w = make_problem(K + B, B, HW, HW, C, K)
+    y = getattr(torch.ops.depthwise, op)(to_dev(x), to_dev(w))
+    torch.cuda.synchronize()
+    assert y.is_contiguous(memory_format=torch.channels_last)
+    exact, _ = oracle_mod.dw_forward(x, w)
+    check(oracle_mod, y, exact, op)
+
+
+REPL = [("conv_56_128_31", 56, 128, 31), ("conv_28_256_29", 28, 256, 29), ("conv_14_512_27", 14, 512, 27),
+        ("conv_7_1024_13", 7, 1024, 13)]
+
+
+@pytest.mark.parametrize("op,HW,C,K", REPL, ids=[r[0] for r in REPL])
+@pytest.mark.parametrize("with_bias", [True, False])
+def test_replknet_ops(eng, oracle_mod, op, HW, C, K, with_bias):
+    x, w = make_problem(K, 2, HW, HW, C, K)
+    b = (np.random.default_rng(K).standard_normal(C) * 0.1).astype(np.float16)
+    bias = to_dev(b) if with_bias else torch.empty(0, dtype=torch.float16, device="cuda")
+    y = getattr(torch.ops.replknet_dw, op)(to_dev(x), to_dev(w), bias)
+    torch.cuda.synchronize()
+    exact, _ = oracle_mod.dw_forward(x, w, b if with_bias else None)
+    check(oracle_mod, y, exact, op)
+
+
+def test_fixed_ops_reject_wrong_shapes_with_runtime_error(eng):
+    x = torch.zeros(1, 768, 16, 16, dtype=torch.float16, device="cuda").contiguous(memory_format=torch.channels_last)
+    w = torch.zeros(7, 7, 768, dtype=torch.float16, device="cuda")
+    with pytest.raises(RuntimeError):
+        torch.ops.depthwise.conv2d_32_768_7(x, w)  # reference: prints and exit(1)
+    x2 = torch.zeros(1, 128, 56, 56, dtype=torch.float16, device="cuda")  # NCHW, not channels_last
+    w2 = torch.zeros(31, 31, 128, dtype=torch.float16, device="cuda")
+    with pytest.raises(RuntimeError):
+        torch.ops.replknet_dw.conv_56_128_31(x2, w2, torch.empty(0, dtype=torch.float16, device="cuda"))
+    with pytest.raises(RuntimeError):
+        torch.ops.depthwise.conv2d_nhwc(x.float(), w)
+
+
+def test_c_abi_direct_call(eng, oracle_mod):
+    """The C entry point a non-Python host would bind, with raw device pointers."""
+    from depthwise_conv_b200 import _lib
+    x, w = make_problem(1, 2, 28, 28, 256, 29)
+    xd, wd = to_dev(x), to_dev(w)
+    y = torch.empty_like(xd)
+    lib = _lib.load()
+    rc = lib.dwb_depthwise_29x29_256_nhwc(xd.data_ptr(), wd.data_ptr(), None, y.data_ptr(), 2, 256, 28, 28,
+                                          torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    exact, _ = oracle_mod.dw_forward(x, w)
+    check(oracle_mod, y, exact)
+    # bad shape / alignment are statuses, not crashes
+    assert lib.dwb_depthwise_29x29_256_nhwc(xd.data_ptr(), wd.data_ptr(), None, y.data_ptr(), 2, 256, 27, 28,
+                                            None) == _lib.ERR_BAD_SHAPE
+    assert lib.dwb_conv2d_nhwc_fwd(xd.data_ptr() + 2, wd.data_ptr(), y.data_ptr(), 2, 28, 28, 256, 29,
+                                   None) == _lib.ERR_BAD_ALIGN
+
+
+def test_custom_module_and_swapper(eng, oracle_mod):
+    from depthwise_conv_b200.depthwise_torch_ops import replace_depthwise_convs
+    torch.manual_seed(0)
+    conv = nn.Conv2d(1536, 1536, 9, groups=1536, padding=4).cuda()
+    model = nn.Sequential(conv)
+    x = torch.randn(2, 1536, 32, 32, device="cuda").half().contiguous(memory_format=torch.channels_last)
+    with torch.no_grad():
+        ref = conv.double()(x.double()).float()
+    conv.float()
+    replace_depthwise_convs(model, verbose=False)
+    with torch.no_grad():
+        y = model(x)
+    torch.cuda.synchronize()
+    # weights went through an fp16 cast in the swap, so compare with a relative bar on fp32 reference
+    err = (y.float() - ref).abs()
+    assert err.max().item() < 2e-2
+    assert (err.norm() / ref.norm()).item() < 2e-3
+
+
+def test_replknet_swapper_stage3(eng):
+    from depthwise_conv_b200.depthwise_replknet_nhwc_ops import replace_replknet_depthwise_nhwc
+    m = nn.Sequential(nn.Conv2d(1024, 1024, 13, groups=1024, padding=6, bias=False)).cuda()
+    x = torch.randn(1, 1024, 7, 7, device="cuda").half().contiguous(memory_format=torch.channels_last)
+    with torch.no_grad():
+        ref = m.float()(x.float())
+    replace_replknet_depthwise_nhwc(m, verbose=False)
+    with torch.no_grad():
+        y = m(x)
+    assert ((y.float() - ref).norm() / ref.norm()).item() < 2e-3
+
+
+class _Block(nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.w = nn.Parameter(torch.randn(9, 9, 256, dtype=torch.float16) / 9)
+        self.b = nn.Parameter(torch.randn(256, dtype=torch.float16) * 0.1)
+        self.s = nn.Parameter(torch.rand(256, dtype=torch.float16) + 0.5)
+        self.t = nn.Parameter(torch.randn(256, dtype=torch.float16) * 0.1)
+
+    def forward(self, x):
+        y = torch.ops.depthwise.conv2d_nhwc_fused(x, self.w, self.b, self.s, self.t, x, 2)
+        return torch.ops.depthwise.conv2d_nhwc(y * 0.5 + 1.0, self.w, None)
+
+
+@pytest.mark.parametrize("mode", ["default", "reduce-overhead"])
+def test_torch_compile_modes_and_replay(eng, mode):
+    torch.manual_seed(0)
+    blk = _Block().cuda()
+    mk = lambda: torch.randn(2, 256, 32, 32, device="cuda").half().contiguous(memory_format=torch.channels_last)  # noqa: E731
+    compiled = torch.compile(blk, mode=mode, fullgraph=True)
+    with torch.no_grad():
+        x1, x2 = mk(), mk()
+        y1 = compiled(x1).clone()
+        y2 = compiled(x2).clone()
+        r1, r2 = blk(x1), blk(x2)
+        assert (y1 - r1).abs().max().item() == 0.0
+        assert (y2 - r2).abs().max().item() == 0.0
+        assert (y1 - y2).abs().max().item() > 0.1
+        # replay follows a changing input (verify_e5b_correctness.py:30-37)
+        outs = [compiled(mk()).clone() for _ in range(5)]
+        diffs = [(outs[i] - outs[i + 1]).abs().max().item() for i in range(4)]
+        assert all(d > 0.1 for d in diffs)
+        again = compiled(x1).clone()
+        assert (again - y1).abs().max().item() == 0.0
+
+
+def test_cuda_graph_capture_of_c_abi(eng, oracle_mod):
+    x, w = make_problem(3, 2, 32, 32, 512, 13)
+    xd, wd = to_dev(x), to_dev(w)
+    y = torch.empty_like(xd)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        eng.conv2d_nhwc_fused(xd, wd, out=y)  # warm-up (device init, attributes) outside capture
+    s.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        eng.conv2d_nhwc_fused(xd, wd, out=y)
+    y.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    exact, _ = oracle_mod.dw_forward(x, w)
+    check(oracle_mod, y, exact, "graph replay")
+    # new data in the captured input buffer is picked up
+    x2, _ = make_problem(4, 2, 32, 32, 512, 13)
+    xd.copy_(to_dev(x2))
+    g.replay()
+    torch.cuda.synchronize()
+    exact2, _ = oracle_mod.dw_forward(x2, w)
+    check(oracle_mod, y, exact2, "graph replay 2")
+
+
+def test_probe_fma_peak_reports_plausible_rates(eng):
+    h, f = eng.probe_fma_peak()
+    assert 10.0 < h < 200.0 and 10.0 < f < 200.0
+
+
+def test_device_error_word_clear(eng):
+    assert eng.device_error() == 0

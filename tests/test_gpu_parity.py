@@ -1,0 +1,256 @@
+"""Parity of the sm_100a engine with the CPU oracle (GPU).
+
+Bar (north star): max |err| <= 1e-2 and rel-L2 <= 1e-3 against the exact
+result for fp16 outputs.  The engine accumulates in fp32, so the default
+path is also held to a much tighter bound: within 2 fp16 ulps of the
+correctly rounded exact value.
+"""
+from __future__ import annotations
+
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import make_problem
+
+pytestmark = pytest.mark.gpu
+
+MAX_TOL, REL_TOL = 1e-2, 1e-3
+
+
+@pytest.fixture(scope="module")
+def eng():
+    import depthwise_conv_b200 as d
+    return d
+
+
+def to_dev(a):
+    """NHWC numpy fp16 -> channels_last [B,C,H,W] CUDA tensor (or 1-D / [K,K,C] as is)."""
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    return t.permute(0, 3, 1, 2) if t.dim() == 4 else t
+
+
+def to_host(t):
+    return t.permute(0, 2, 3, 1).contiguous().cpu().numpy() if t.dim() == 4 else t.cpu().numpy()
+
+
+def ulp16(v):
+    """Spacing of fp16 numbers at |v| (subnormal spacing floor)."""
+    a = np.abs(np.asarray(v, np.float64))
+    e = np.floor(np.log2(np.maximum(a, 2.0 ** -14)))
+    return 2.0 ** (e - 10)
+
+
+def assert_parity(O, y_dev, exact, tight=True, what=""):
+    y = to_host(y_dev).astype(np.float64)
+    max_err, rel = O.parity(y, exact)
+    assert max_err <= MAX_TOL and rel <= REL_TOL, f"{what}: max {max_err:.3e} rel {rel:.3e}"
+    if tight:
+        err = np.abs(y - exact)
+        bad = err > 2.0 * ulp16(exact) + 1e-6
+        assert not bad.any(), f"{what}: {bad.sum()} outputs beyond 2 ulp (max {err.max():.3e})"
+    return max_err, rel
+
+
+def run_engine(eng, x, w, bias=None, scale=None, shift=None, residual=False, act="none", accum=0):
+    xd = to_dev(x)
+    wd = to_dev(w)
+    bd = to_dev(bias) if bias is not None else None
+    sd = to_dev(scale) if scale is not None else None
+    hd = to_dev(shift) if shift is not None else None
+    y = eng.conv2d_nhwc_fused(xd, wd, bd, sd, hd, xd if residual else None, act, accum)
+    torch.cuda.synchronize()
+    return y
+
+
+# ---------------------------------------------------------------- golden vectors
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "dw_cases.npz")
+
+
+def _golden():
+    z = np.load(GOLDEN)
+    meta = json.loads(str(z["__meta__"]))
+    out = []
+    for m in meta:
+        c = {k.split("__", 1)[1]: z[k] for k in z.files if k.startswith(m["name"] + "__")}
+        c.update(m)
+        out.append(c)
+    return out
+
+
+@pytest.mark.parametrize("case", _golden(), ids=lambda c: c["name"])
+def test_golden_vectors(eng, oracle_mod, case):
+    f16 = lambda a: np.asarray(a).view(np.float16)  # noqa: E731
+    act = {0: "none", 1: "relu", 2: "gelu"}[int(case["act"])] if "act" in case else "none"
+    y = run_engine(eng, f16(case["x"]), f16(case["w"]), f16(case["bias"]) if "bias" in case else None,
+                   f16(case["scale"]) if "scale" in case else None, f16(case["shift"]) if "shift" in case else None,
+                   "residual" in case, act)
+    assert_parity(oracle_mod, y, case["y"], what=case["name"])
+
+
+# ---------------------------------------------------------------- shape sweep
+
+SWEEP = []
+for _K in range(1, 32, 2):
+    SWEEP.append((1, 7 + _K % 5, 9 + _K % 3, 64, _K))    # one channel block; image smaller than K for big K
+    SWEEP.append((2, 23, 17, 72, _K))                    # ragged channel block (72 = 64 + 8)
+SWEEP += [(1, 1, 1, 8, 7), (3, 2, 40, 16, 9), (1, 40, 2, 24, 31), (1, 61, 70, 136, 5), (2, 33, 65, 128, 15),
+          (1, 100, 3, 8, 3), (1, 5, 130, 64, 11)]
+
+
+@pytest.mark.parametrize("B,H,W,C,K", SWEEP)
+def test_shape_sweep_fp32(eng, oracle_mod, B, H, W, C, K):
+    x, w = make_problem(100 + K + H, B, H, W, C, K)
+    exact, _ = oracle_mod.dw_forward(x, w)
+    y = run_engine(eng, x, w)
+    assert_parity(oracle_mod, y, exact, what=f"{(B, H, W, C, K)}")
+
+
+@pytest.mark.parametrize("K", [3, 7, 9, 13, 17, 21, 27, 29, 31])
+def test_mixed_accumulation_within_bar(eng, oracle_mod, K):
+    x, w = make_problem(7 + K, 1, 30, 33, 64, K)
+    exact, _ = oracle_mod.dw_forward(x, w)
+    y = run_engine(eng, x, w, accum=1)
+    assert_parity(oracle_mod, y, exact, tight=False, what=f"mixed K={K}")
+
+
+# ---------------------------------------------------------------- fused epilogue
+
+@pytest.mark.parametrize("act", ["none", "relu", "gelu"])
+@pytest.mark.parametrize("terms", ["bias", "bias_bn", "bias_bn_res", "bn_res"])
+def test_fused_epilogue(eng, oracle_mod, act, terms):
+    B, H, W, C, K = 2, 19, 21, 128, 9
+    x, w = make_problem(31, B, H, W, C, K)
+    rng = np.random.default_rng(9)
+    bias = (rng.standard_normal(C) * 0.2).astype(np.float16) if "bias" in terms else None
+    scale = (rng.uniform(0.5, 1.5, C)).astype(np.float16) if "bn" in terms else None
+    shift = (rng.standard_normal(C) * 0.2).astype(np.float16) if "bn" in terms else None
+    res = "res" in terms
+    exact, _ = oracle_mod.dw_forward(x, w, bias, scale, shift, x if res else None, act)
+    y = run_engine(eng, x, w, bias, scale, shift, res, act)
+    assert_parity(oracle_mod, y, exact, what=f"{terms}/{act}")
+
+
+# ---------------------------------------------------------------- BASELINE configs
+
+B1_CONFIGS = [  # (name, B, H, W, C, K, weight std)
+    ("convmixer768_dw", 1, 32, 32, 768, 7, 0.02),
+    ("convmixer1536_dw", 1, 32, 32, 1536, 9, 0.02),
+    ("replknet_c3", 1, 56, 56, 128, 31, None),
+    ("replknet_c4", 1, 28, 28, 256, 29, None),
+    ("replknet_c5", 1, 14, 14, 512, 27, None),
+    ("replknet_c6", 1, 7, 7, 1024, 13, None),
+    ("bsweep_b1", 1, 32, 32, 1536, 9, 1.0 / 9),
+]
+
+
+@pytest.mark.parametrize("name,B,H,W,C,K,ws", B1_CONFIGS, ids=[c[0] for c in B1_CONFIGS])
+def test_baseline_batch1_configs_full(eng, oracle_mod, name, B, H, W, C, K, ws):
+    x, w = make_problem(0, B, H, W, C, K, wscale=ws)
+    exact, _ = oracle_mod.dw_forward(x, w)
+    y = run_engine(eng, x, w)
+    assert_parity(oracle_mod, y, exact, what=name)
+
+
+def _sampled_check(eng, oracle_mod, B, H, W, C, K, act="none", npix=1536, seed=0, with_epi=False):
+    """Full-size problem, checked at sampled pixels (all borders of two images) and by channel sums."""
+    x, w = make_problem(seed, B, H, W, C, K)
+    bias = scale = shift = None
+    if with_epi:
+        bias = np.zeros(C, np.float16)
+        scale = np.full(C, 1.0 / np.sqrt(1.0 + 1e-5), np.float16)
+        shift = np.zeros(C, np.float16)
+    y = to_host(run_engine(eng, x, w, bias, scale, shift, False, act)).reshape(-1, C)
+    rng = np.random.default_rng(seed + 1)
+    border = [(b * H + h) * W + c for b in (0, B - 1) for h in range(H) for c in range(W)
+              if h in (0, H - 1) or c in (0, W - 1)]
+    pix = np.unique(np.concatenate([rng.integers(0, B * H * W, npix), np.array(border, np.int64)]))
+    exact, _ = oracle_mod.dw_forward_pixels(x, w, pix, bias, scale, shift, None, act)
+    max_err, rel = oracle_mod.parity(y[pix].astype(np.float64), exact)
+    assert max_err <= MAX_TOL and rel <= REL_TOL, f"sampled: max {max_err:.3e} rel {rel:.3e}"
+    if not with_epi:
+        # size-independent property: per-channel sums over whole images
+        sums = oracle_mod.channel_sums(x[[0, B - 1]], w)
+        yimg = y.reshape(B, H * W, C)[[0, B - 1]].astype(np.float64)
+        ysum = yimg.sum(axis=1)
+        # fp16 output rounding adds a random walk of H*W half-ulps per channel
+        rms = np.sqrt((yimg ** 2).mean())
+        tol = 8.0 * np.sqrt(H * W) * rms * 2.0 ** -11 + 1e-3
+        dev = np.abs(ysum - sums).max()
+        assert dev <= tol, f"channel sums off by {dev:.3e} > {tol:.3e}"
+
+
+@pytest.mark.parametrize("B", [16, 64, 256])
+def test_batch_sweep_sampled(eng, oracle_mod, B):
+    _sampled_check(eng, oracle_mod, B, 32, 32, 1536, 9, seed=B)
+
+
+@pytest.mark.parametrize("K", [7, 9, 13, 17, 21, 27, 29, 31])
+def test_kernel_size_sweep_sampled_with_epilogue(eng, oracle_mod, K):
+    _sampled_check(eng, oracle_mod, 64, 56, 56, 1024, K, act="gelu", npix=512, seed=K, with_epi=True)
+
+
+@pytest.mark.parametrize("K", [9, 31])
+def test_kernel_size_sweep_channel_sums(eng, oracle_mod, K):
+    _sampled_check(eng, oracle_mod, 8, 56, 56, 1024, K, npix=256, seed=50 + K)
+
+
+# ---------------------------------------------------------------- memory safety
+
+def test_output_guard_regions_untouched(eng, oracle_mod):
+    B, H, W, C, K = 2, 13, 11, 72, 9
+    x, w = make_problem(77, B, H, W, C, K)
+    n = B * H * W * C
+    guard = 4096
+    buf = torch.full((n + 2 * guard,), 12345.0, dtype=torch.float16, device="cuda")
+    y = buf[guard:guard + n].view(B, H, W, C).permute(0, 3, 1, 2)
+    eng.conv2d_nhwc_fused(to_dev(x), to_dev(w), out=y)
+    torch.cuda.synchronize()
+    assert torch.all(buf[:guard] == 12345.0) and torch.all(buf[guard + n:] == 12345.0)
+    exact, _ = oracle_mod.dw_forward(x, w)
+    assert_parity(oracle_mod, y, exact)
+
+
+def test_residual_reads_stay_in_bounds(eng, oracle_mod):
+    # NaN guards around the residual: an out-of-bounds read would poison the output
+    B, H, W, C, K = 1, 9, 10, 64, 7
+    x, w = make_problem(78, B, H, W, C, K)
+    n = B * H * W * C
+    guard = 2048
+    buf = torch.full((n + 2 * guard,), float("nan"), dtype=torch.float16, device="cuda")
+    buf[guard:guard + n] = torch.from_numpy(x.reshape(-1)).cuda()
+    res = buf[guard:guard + n].view(B, H, W, C).permute(0, 3, 1, 2)
+    y = eng.conv2d_nhwc_fused(to_dev(x), to_dev(w), residual=res)
+    torch.cuda.synchronize()
+    exact, _ = oracle_mod.dw_forward(x, w, residual=x)
+    assert_parity(oracle_mod, y, exact)
+
+
+def test_no_device_error_recorded(eng):
+    assert eng.device_error(clear=True) == 0
+
+
+# ---------------------------------------------------------------- streams / edge cases
+
+def test_runs_on_current_stream(eng, oracle_mod):
+    x, w = make_problem(5, 4, 32, 32, 256, 9)
+    exact, _ = oracle_mod.dw_forward(x, w)
+    xd, wd = to_dev(x), to_dev(w)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        y = eng.conv2d_nhwc(xd, wd)
+        y2 = y * 1.0  # consumer on the same stream
+    s.synchronize()
+    assert_parity(oracle_mod, y2, exact)
+
+
+def test_zero_batch_is_noop(eng):
+    xd = torch.empty(0, 64, 8, 8, dtype=torch.float16, device="cuda").contiguous(memory_format=torch.channels_last)
+    wd = torch.zeros(7, 7, 64, dtype=torch.float16, device="cuda")
+    y = eng.conv2d_nhwc(xd, wd)
+    assert y.shape == xd.shape
