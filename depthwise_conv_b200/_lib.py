@@ -44,7 +44,7 @@ class Plan(ctypes.Structure):
                 ("tile_h", ctypes.c_int32), ("tile_w", ctypes.c_int32), ("tile_w_in", ctypes.c_int32),
                 ("ring_rows", ctypes.c_int32), ("ring_wrows", ctypes.c_int32), ("consumer_warps", ctypes.c_int32),
                 ("threads", ctypes.c_int32), ("smem_bytes", ctypes.c_int32), ("ctas_per_sm", ctypes.c_int32),
-                ("grid", ctypes.c_int64), ("accum", ctypes.c_int32), ("regs_estimate", ctypes.c_int32),
+                ("grid", ctypes.c_int64), ("tiles", ctypes.c_int64), ("accum", ctypes.c_int32), ("regs_estimate", ctypes.c_int32),
                 ("model_cost", ctypes.c_double)]
 
     def as_dict(self) -> dict:

@@ -75,6 +75,7 @@ struct VariantState {
   int regs = -1;         // -1 unknown, 0 unavailable
   bool smem_set = false;
   int smem_max = 0;
+  int occ_threads = 0, occ_smem = -1, occ_ctas = 0;  // last occupancy query
 };
 
 using PlanKey = std::tuple<long long, long long, long long, long long, int, int>;  // B, H, W, C, K, accum
@@ -228,6 +229,16 @@ static int encode_w_map(CUtensorMap* m, const void* w, long long C, int K) {
 
 static inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Mixed accumulation: kernel rows per fp16 chain.  A chain of L fp16
+// roundings leaves a relative error of about 2e-4 * sqrt(L / 2) (random
+// walk of half-ulp roundings); chains stay at <= 24 taps (K >= 25 rows are
+// split in two by the kernel itself).
+static int mixed_chain_rows(int K) {
+  if (K >= 25) return 1;
+  const int rows = 24 / K;
+  return rows > 3 ? 3 : rows;
+}
+
 // Argument checks shared by every entry point (no CUDA calls).  An empty
 // batch is accepted before the pointer checks: an empty tensor may report a
 // null data pointer.
@@ -288,6 +299,8 @@ static int launch_plan(DeviceState* st, const dwb_plan& plan, const void* x, con
   p.tiles_h = static_cast<int>((H + plan.tile_h - 1) / plan.tile_h);
   p.tiles_w = static_cast<int>((W + plan.tile_w - 1) / plan.tile_w);
   p.cblocks = static_cast<int>((C + kChannelsPerCta - 1) / kChannelsPerCta);
+  if (plan.tiles > 0x7fffffffLL) return DWB_ERR_BAD_SHAPE;
+  p.num_tiles = static_cast<uint32_t>(plan.tiles);
   p.ncg = plan.tile_w / plan.cols_per_thread;
   p.consumer_warps = plan.consumer_warps;
   p.ring_rows = plan.ring_rows;
@@ -296,9 +309,32 @@ static int launch_plan(DeviceState* st, const dwb_plan& plan, const void* x, con
   p.x_ring_off = kBarrierBytes;
   p.w_ring_off = kBarrierBytes + static_cast<uint32_t>(plan.ring_rows) * plan.tile_w_in * kPixelBytes;
   p.err = st->err_word;
+  p.chain_rows = mixed_chain_rows(K);
+
+  // grid < 0: persistent, as many CTAs as fit on the device at once (measured
+  // by the occupancy calculator for this variant); otherwise the plan's CTA
+  // count (one tile per CTA when it equals the tile count).
+  long long grid = plan.grid;
+  {
+    VariantState& vs = st->variants[variant_slot(e->k, e->r, e->m, e->acc)];
+    std::lock_guard<std::mutex> lk(st->mu);
+    if (vs.occ_threads != plan.threads || vs.occ_smem != plan.smem_bytes) {
+      int occ = 0;
+      const cudaError_t oe =
+          cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, e->fn, plan.threads, static_cast<size_t>(plan.smem_bytes));
+      if (oe != cudaSuccess) return cuda_fail("cudaOccupancyMaxActiveBlocksPerMultiprocessor", oe);
+      vs.occ_threads = plan.threads;
+      vs.occ_smem = plan.smem_bytes;
+      vs.occ_ctas = occ;
+    }
+    if (vs.occ_ctas < 1) return DWB_ERR_UNSUPPORTED;
+    const long long fit = static_cast<long long>(vs.occ_ctas) * st->hw.sm_count;
+    if (grid < 0) grid = fit;
+    if (grid <= 0 || grid > plan.tiles) grid = plan.tiles;
+  }
 
   void* args[3] = {&tmx, &tmw, &p};
-  const cudaError_t ce = cudaLaunchKernel(e->fn, dim3(static_cast<unsigned>(plan.grid)), dim3(plan.threads), args,
+  const cudaError_t ce = cudaLaunchKernel(e->fn, dim3(static_cast<unsigned>(grid)), dim3(plan.threads), args,
                                           static_cast<size_t>(plan.smem_bytes), static_cast<cudaStream_t>(stream));
   if (ce != cudaSuccess) {
     (void)cudaGetLastError();

@@ -65,6 +65,19 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return true;
 }
 
+// Position in a ring of mbarrier-guarded slots: the slot index and the
+// parity of the current use of that slot (flips at every wrap).
+struct RingPos {
+  int slot = 0;
+  uint32_t phase = 0;
+  __device__ __forceinline__ void next(int n) {
+    if (++slot == n) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -97,12 +110,41 @@ __device__ __forceinline__ float2 bits_f2(unsigned long long b) {
   return make_float2(__uint_as_float(static_cast<uint32_t>(b)), __uint_as_float(static_cast<uint32_t>(b >> 32)));
 }
 
+// Packed fp32 pairs are kept in 64-bit registers ({lo, hi} = two channels)
+// from conversion to epilogue, so no instruction ever repacks them.
+typedef unsigned long long f32x2;
+
 // acc += a * b, element-wise on the two lanes, each a single-rounding fp32 FMA.
-__device__ __forceinline__ void ffma2(float2& acc, const float2& a, const float2& b) {
-  unsigned long long c = f2_bits(acc);
-  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(c) : "l"(f2_bits(a)), "l"(f2_bits(b)));
-  acc = bits_f2(c);
+__device__ __forceinline__ void ffma2(f32x2& acc, f32x2 a, f32x2 b) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
 }
+
+// half2 (two channels) -> packed fp32 pair.
+__device__ __forceinline__ f32x2 h2_to_f32x2(__half2 h) {
+  f32x2 r;
+  const uint32_t u = *reinterpret_cast<const uint32_t*>(&h);
+  asm("{\n\t.reg .b16 lo, hi;\n\t.reg .f32 a, b;\n\t"
+      "mov.b32 {lo, hi}, %1;\n\tcvt.f32.f16 a, lo;\n\tcvt.f32.f16 b, hi;\n\t"
+      "mov.b64 %0, {a, b};\n\t}"
+      : "=l"(r)
+      : "r"(u));
+  return r;
+}
+
+__device__ __forceinline__ float2 f32x2_unpack(f32x2 v) { return bits_f2(v); }
+
+// acc.{lo,hi} += h.{lo,hi} with mixed-precision adds (fp16 operand, fp32
+// accumulator, one rounding each).
+__device__ __forceinline__ void add_h2_to_f32x2(f32x2& acc, __half2 h) {
+  const uint32_t u = *reinterpret_cast<const uint32_t*>(&h);
+  asm("{\n\t.reg .b16 lo, hi;\n\t.reg .f32 a, b;\n\t"
+      "mov.b32 {lo, hi}, %1;\n\tmov.b64 {a, b}, %0;\n\t"
+      "add.rn.f32.f16 a, lo, a;\n\tadd.rn.f32.f16 b, hi, b;\n\t"
+      "mov.b64 %0, {a, b};\n\t}"
+      : "+l"(acc)
+      : "r"(u));
+}
+__device__ __forceinline__ f32x2 f32x2_zero() { return 0ull; }
 
 // ---- epilogue ---------------------------------------------------------------
 

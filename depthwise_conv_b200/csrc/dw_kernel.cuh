@@ -1,31 +1,39 @@
 // dw_kernel.cuh -- the row-streaming depthwise convolution kernel for sm_100a.
 //
 // Work decomposition
-//   CTA  = one output tile: tile_h rows x tile_w columns x 64 channels of one
+//   tile = tile_h output rows x tile_w output columns x 64 channels of one
 //          image (channels past C are zero-filled by TMA and never stored).
+//   CTA  = persistent: it walks the tiles blockIdx.x, blockIdx.x + gridDim.x,
+//          ... so the loads of the next tile overlap the last steps and the
+//          epilogue of the current one.
 //   warp = one "slot" of the tile: M consecutive output rows x R consecutive
 //          output columns x 64 channels; lane l owns channels (2l, 2l+1), so
 //          every shared-memory access of a warp is one contiguous 128-byte row
 //          (conflict-free) and every row/column skip is warp-uniform.
-//   thread accumulators: acc[M][R] float2 (two channels), fp32 throughout.
+//   thread accumulators: acc[M][R], packed fp32 pairs.
 //
 // Data movement (no multicast, plain per-CTA TMA tile loads)
 //   The kernel walks the kernel rows ki (step s).  At step s every output row
 //   h of the tile reads input row h - pad + s, so the tile needs the input
 //   rows [h0 - pad + s, h0 - pad + s + tile_h): a window that slides one row
 //   per step.  A dedicated producer warp streams those rows, and weight row
-//   ki, through two shared-memory rings guarded by full/empty mbarriers:
+//   ki, through two shared-memory rings guarded by full/empty mbarriers; the
+//   rings run continuously across the CTA's tiles:
 //     input row  : [tile_w + K - 1 columns][64 channels] fp16 (zero padding
 //                  comes from TMA out-of-bounds fill)
 //     weight row : [K taps][64 channels] fp16
-//   Steps whose input rows all fall outside the image are not executed.
+//   Kernel rows whose input rows all fall outside the image are skipped.
 //
 // Inner loop (weight-stationary per kernel row)
-//   The K weights of row ki are converted once to float2 registers; then for
-//   each of the M rows the thread slides along R + K - 1 input columns: each
-//   input half2 is loaded and converted once and feeds up to R accumulators
-//   through packed fp32x2 FMAs (ACC = 0), or fp16x2 HFMA2 into a per-row
-//   partial that is added to the fp32 accumulator after the row (ACC = 1).
+//   The K weights of row ki are held in registers; then the thread slides
+//   along R + K - 1 input columns of its M rows at once (the rows are
+//   interleaved so each weight register feeds M independent chains): each
+//   input half2 is loaded once and feeds up to R outputs.
+//     ACC = 0: inputs and weights converted to fp32, packed fp32x2 FMAs
+//              (FFMA2) into fp32 accumulators -- every tap in fp32;
+//     ACC = 1: fp16x2 HFMA2 into short fp16 chains (chain_rows kernel rows,
+//              or half a row for K >= 25) that are added to the fp32
+//              accumulators when they end -- no conversion in the loop.
 //
 // Epilogue (fused): v = acc + bias; v = act(v); v = v * scale + shift;
 //   v += residual; stored as half2, 128 contiguous bytes per warp.
@@ -49,19 +57,107 @@ struct DwParams {
   int B, H, W, C;
   int tile_h, tile_w, tile_w_in;
   int tiles_h, tiles_w, cblocks;
+  uint32_t num_tiles;      // < 2^31 (checked by the launcher)
   int ncg;                 // column groups (warps across the tile width)
   int consumer_warps;
   int ring_rows, ring_wrows;
   int act;
   uint32_t x_ring_off, w_ring_off;  // byte offsets inside dynamic smem
   int* err;                         // device error word (bounded-wait expiry)
+  int chain_rows;                   // mixed mode: kernel rows per fp16 chain
 };
+
+// Geometry of one tile.
+struct TileInfo {
+  int b, h0, w0, c0;
+  int s_lo;    // first kernel row with an in-image input row
+  int nsteps;  // kernel rows executed
+  int nrows;   // input rows streamed = nsteps + tile_h - 1
+};
+
+template <int K>
+__device__ __forceinline__ TileInfo decode_tile(const DwParams& p, uint32_t t) {
+  constexpr int PAD = K / 2;
+  TileInfo ti;
+  // tile-row fastest so CTAs working at the same time share halo rows in L2
+  uint32_t q = t / static_cast<uint32_t>(p.tiles_h);
+  const int th = static_cast<int>(t - q * static_cast<uint32_t>(p.tiles_h));
+  t = q;
+  q = t / static_cast<uint32_t>(p.tiles_w);
+  const int tw = static_cast<int>(t - q * static_cast<uint32_t>(p.tiles_w));
+  t = q;
+  q = t / static_cast<uint32_t>(p.cblocks);
+  const int cbk = static_cast<int>(t - q * static_cast<uint32_t>(p.cblocks));
+  ti.b = static_cast<int>(q);
+  ti.h0 = th * p.tile_h;
+  ti.w0 = tw * p.tile_w;
+  ti.c0 = cbk * kChannelsPerCta;
+  const int rows_in_tile = min(p.tile_h, p.H - ti.h0);
+  ti.s_lo = max(0, PAD - (ti.h0 + rows_in_tile - 1));
+  const int s_hi = min(K, p.H + PAD - ti.h0);
+  ti.nsteps = s_hi - ti.s_lo;  // >= 1 because h0 < H
+  ti.nrows = ti.nsteps + p.tile_h - 1;
+  return ti;
+}
+
+// One kernel row for the warp's M rows (row m reads xrow[m]; rows whose
+// input row lies outside the image are skipped, warp-uniformly).
+template <int K, int R, int M, int ACC>
+__device__ __forceinline__ void step_rows(f32x2 (&acc)[M][R], __half2 (&part)[M][(ACC == 1 && K >= 25) ? 2 : 1][R],
+                                          const __half2* __restrict__ wrow, const __half2* __restrict__ xrow0,
+                                          const __half2* __restrict__ xrow1, bool v0, bool v1) {
+  constexpr int NJ = R + K - 1;
+  constexpr int SPLIT = (ACC == 1 && K >= 25) ? 2 : 1;
+  if constexpr (ACC == 0) {
+    f32x2 wv[K];
+#pragma unroll
+    for (int kj = 0; kj < K; ++kj) wv[kj] = h2_to_f32x2(wrow[kj * kPixelH2]);
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      if (m == 0 ? v0 : v1) {
+        const __half2* xrow = m == 0 ? xrow0 : xrow1;
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+          const f32x2 xv = h2_to_f32x2(xrow[j * kPixelH2]);
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const int kj = j - r;
+            if (kj >= 0 && kj < K) ffma2(acc[m][r], xv, wv[kj]);
+          }
+        }
+      }
+    }
+  } else {
+    __half2 wv[K];
+#pragma unroll
+    for (int kj = 0; kj < K; ++kj) wv[kj] = wrow[kj * kPixelH2];
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      if (m == 0 ? v0 : v1) {
+        const __half2* xrow = m == 0 ? xrow0 : xrow1;
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+          const __half2 xv = xrow[j * kPixelH2];
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const int kj = j - r;
+            if (kj >= 0 && kj < K) {
+              const int c = (SPLIT == 2 && kj >= K / 2 + 1) ? 1 : 0;
+              part[m][c][r] = __hfma2(xv, wv[kj], part[m][c][r]);
+            }
+          }
+        }
+      }
+    }
+  }
+}
 
 template <int K, int R, int M, int ACC>
 __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                  const __grid_constant__ CUtensorMap tmap_w, const DwParams p) {
   constexpr int PAD = K / 2;
   constexpr int NJ = R + K - 1;  // input columns a thread slides over
+  constexpr int SPLIT = (ACC == 1 && K >= 25) ? 2 : 1;
   extern __shared__ __align__(1024) unsigned char smem[];
 
   const int RR = p.ring_rows;
@@ -78,25 +174,6 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Tile decode: tile-row fastest so consecutive CTAs share halo rows in L2.
-  long long t = blockIdx.x;
-  const int th = static_cast<int>(t % p.tiles_h);
-  t /= p.tiles_h;
-  const int tw = static_cast<int>(t % p.tiles_w);
-  t /= p.tiles_w;
-  const int cbk = static_cast<int>(t % p.cblocks);
-  const int b = static_cast<int>(t / p.cblocks);
-  const int h0 = th * p.tile_h;
-  const int w0 = tw * p.tile_w;
-  const int c0 = cbk * kChannelsPerCta;
-  const int rows_in_tile = min(p.tile_h, p.H - h0);
-
-  // Kernel-row range with at least one in-image input row for this tile.
-  const int s_lo = max(0, PAD - (h0 + rows_in_tile - 1));
-  const int s_hi = min(K, p.H + PAD - h0);
-  const int nsteps = s_hi - s_lo;
-  const int nrows = nsteps + p.tile_h - 1;  // streamed input rows
-
   if (threadIdx.x == 0) {
     for (int i = 0; i < RR; ++i) {
       mbar_init(&full_x[i], 1);
@@ -112,30 +189,39 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
 
   if (warp == p.consumer_warps) {
     // ---------------- producer warp ----------------
-    if (lane == 0 && nsteps > 0) {
+    // Issues, in the order the consumers need them, weight row s_lo+st and
+    // the input rows up to st + tile_h - 1 of every tile; a slot is refilled
+    // only after the consumers released its previous use (empty barrier).
+    if (lane == 0) {
       prefetch_tmap(&tmap_x);
       prefetch_tmap(&tmap_w);
-      int q = 0;  // next input row (sequence number) to issue
+      RingPos xr, wr;  // next slot to fill, and the parity of that fill
+      long long xfills = 0, wfills = 0;
       bool ok = true;
-      for (int st = 0; st < nsteps && ok; ++st) {
-        // weight row (s_lo + st)
-        const int ws = st % RW;
-        if (st >= RW) ok = mbar_wait_bounded(&empty_w[ws], ((st / RW) - 1) & 1, p.err, 3);
-        if (!ok) break;
-        mbar_arrive_expect_tx(&full_w[ws], wrow_bytes);
-        tma_load_3d(wring + ws * wrow_bytes, &tmap_w, &full_w[ws], c0, 0, s_lo + st);
-        // input rows needed by this step: q < st + tile_h
-        const int need = min(st + p.tile_h, nrows);
-        for (; q < need; ++q) {
-          const int slot = q % RR;
-          if (q >= RR) ok = mbar_wait_bounded(&empty_x[slot], ((q / RR) - 1) & 1, p.err, 3);
+      for (uint32_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        const TileInfo ti = decode_tile<K>(p, t);
+        int q = 0;  // next input row of this tile
+        for (int st = 0; st < ti.nsteps && ok; ++st) {
+          if (wfills >= RW) ok = mbar_wait_bounded(&empty_w[wr.slot], wr.phase ^ 1u, p.err, 3);
           if (!ok) break;
-          const int abs_row = h0 - PAD + s_lo + q;
-          if (abs_row >= 0 && abs_row < p.H) {
-            mbar_arrive_expect_tx(&full_x[slot], row_bytes);
-            tma_load_4d(xring + slot * row_bytes, &tmap_x, &full_x[slot], c0, w0 - PAD, abs_row, b);
-          } else {
-            mbar_arrive(&full_x[slot]);  // nothing to load: consumers skip this row
+          mbar_arrive_expect_tx(&full_w[wr.slot], wrow_bytes);
+          tma_load_3d(wring + wr.slot * wrow_bytes, &tmap_w, &full_w[wr.slot], ti.c0, 0, ti.s_lo + st);
+          wr.next(RW);
+          ++wfills;
+          const int need = (st + 1 == ti.nsteps) ? ti.nrows : st + p.tile_h;
+          for (; q < need; ++q) {
+            if (xfills >= RR) ok = mbar_wait_bounded(&empty_x[xr.slot], xr.phase ^ 1u, p.err, 3);
+            if (!ok) break;
+            const int abs_row = ti.h0 - PAD + ti.s_lo + q;
+            if (abs_row >= 0 && abs_row < p.H) {
+              mbar_arrive_expect_tx(&full_x[xr.slot], row_bytes);
+              tma_load_4d(xring + xr.slot * row_bytes, &tmap_x, &full_x[xr.slot], ti.c0, ti.w0 - PAD, abs_row,
+                          ti.b);
+            } else {
+              mbar_arrive(&full_x[xr.slot]);  // nothing to load: consumers skip this row
+            }
+            xr.next(RR);
+            ++xfills;
           }
         }
       }
@@ -148,117 +234,129 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
   const int cg = warp - rg * p.ncg;
   const int trow0 = rg * M;  // first tile row of this warp
   const int col0 = cg * R;   // first tile column of this warp
+  const int xoff = col0 * kPixelH2 + lane;  // half2 offset of this thread's first input column
 
-  float2 acc[M][R];
-#pragma unroll
-  for (int m = 0; m < M; ++m)
-#pragma unroll
-    for (int r = 0; r < R; ++r) acc[m][r] = make_float2(0.f, 0.f);
-
+  RingPos wait_x;  // next input row to wait for
+  RingPos wait_w;  // weight row of the current step
+  RingPos rel_x;   // next input row to release
   bool ok = true;
-  for (int st = 0; st < nsteps; ++st) {
-    // Rows [st, st + tile_h) must be resident; earlier ones were waited on.
-    if (st == 0) {
-      for (int q = 0; q < min(p.tile_h, nrows) && ok; ++q) ok = mbar_wait_bounded(&full_x[q % RR], (q / RR) & 1, p.err, 1);
-    } else {
-      const int q = st + p.tile_h - 1;
-      if (q < nrows) ok = mbar_wait_bounded(&full_x[q % RR], (q / RR) & 1, p.err, 1);
-    }
-    if (ok) ok = mbar_wait_bounded(&full_w[st % RW], (st / RW) & 1, p.err, 2);
-    if (!ok) break;
 
-    const int s = s_lo + st;  // kernel row
-    const __half2* wrow = reinterpret_cast<const __half2*>(wring + (st % RW) * wrow_bytes) + lane;
-
-    if constexpr (ACC == 0) {
-      float2 wv[K];
-#pragma unroll
-      for (int kj = 0; kj < K; ++kj) wv[kj] = __half22float2(wrow[kj * kPixelH2]);
-#pragma unroll
-      for (int m = 0; m < M; ++m) {
-        const int out_row = h0 + trow0 + m;
-        const int in_row = out_row - PAD + s;
-        if (out_row < p.H && in_row >= 0 && in_row < p.H) {  // warp-uniform
-          const int q = st + trow0 + m;
-          const __half2* xrow =
-              reinterpret_cast<const __half2*>(xring + (q % RR) * row_bytes) + col0 * kPixelH2 + lane;
-#pragma unroll
-          for (int j = 0; j < NJ; ++j) {
-            const float2 xv = __half22float2(xrow[j * kPixelH2]);
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-              const int kj = j - r;
-              if (kj >= 0 && kj < K) ffma2(acc[m][r], xv, wv[kj]);
-            }
-          }
-        }
-      }
-    } else {
-      __half2 wv[K];
-#pragma unroll
-      for (int kj = 0; kj < K; ++kj) wv[kj] = wrow[kj * kPixelH2];
-#pragma unroll
-      for (int m = 0; m < M; ++m) {
-        const int out_row = h0 + trow0 + m;
-        const int in_row = out_row - PAD + s;
-        if (out_row < p.H && in_row >= 0 && in_row < p.H) {
-          const int q = st + trow0 + m;
-          const __half2* xrow =
-              reinterpret_cast<const __half2*>(xring + (q % RR) * row_bytes) + col0 * kPixelH2 + lane;
-          __half2 part[R];
-#pragma unroll
-          for (int r = 0; r < R; ++r) part[r] = __float2half2_rn(0.f);
-#pragma unroll
-          for (int j = 0; j < NJ; ++j) {
-            const __half2 xv = xrow[j * kPixelH2];
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-              const int kj = j - r;
-              if (kj >= 0 && kj < K) part[r] = __hfma2(xv, wv[kj], part[r]);
-            }
-          }
-#pragma unroll
-          for (int r = 0; r < R; ++r) {
-            const float2 f = __half22float2(part[r]);
-            acc[m][r].x += f.x;
-            acc[m][r].y += f.y;
-          }
-        }
-      }
-    }
-
-    __syncwarp();
-    if (lane == 0) {
-      mbar_arrive(&empty_x[st % RR]);  // row st is never read again
-      mbar_arrive(&empty_w[st % RW]);
-    }
-  }
-  if (!ok) return;  // a bounded wait expired; the error word is set
-
-  // ---------------- fused epilogue ----------------
-  const int c = c0 + 2 * lane;
-  if (c >= p.C) return;
   float2 bias = make_float2(0.f, 0.f), scale = make_float2(1.f, 1.f), shift = make_float2(0.f, 0.f);
-  if (p.bias) bias = __half22float2(*reinterpret_cast<const __half2*>(p.bias + c));
-  if (p.scale) scale = __half22float2(*reinterpret_cast<const __half2*>(p.scale + c));
-  if (p.shift) shift = __half22float2(*reinterpret_cast<const __half2*>(p.shift + c));
+  int bias_c0 = -1;
+
+  for (uint32_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+    const TileInfo ti = decode_tile<K>(p, t);
+
+    f32x2 acc[M][R];  // packed fp32 (channel 2l, channel 2l+1)
 #pragma unroll
-  for (int m = 0; m < M; ++m) {
-    const int h = h0 + trow0 + m;
-    if (h >= p.H) continue;
+    for (int m = 0; m < M; ++m)
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int w = w0 + col0 + r;
-      if (w >= p.W) continue;
-      const long long off = ((static_cast<long long>(b) * p.H + h) * p.W + w) * p.C + c;
-      float vx = apply_act(acc[m][r].x + bias.x, p.act) * scale.x + shift.x;
-      float vy = apply_act(acc[m][r].y + bias.y, p.act) * scale.y + shift.y;
-      if (p.residual) {
-        const float2 res = __half22float2(*reinterpret_cast<const __half2*>(p.residual + off));
-        vx += res.x;
-        vy += res.y;
+      for (int r = 0; r < R; ++r) acc[m][r] = f32x2_zero();
+    __half2 part[M][SPLIT][R];  // mixed mode fp16 chains (unused in fp32 mode)
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+#pragma unroll
+      for (int c = 0; c < SPLIT; ++c)
+#pragma unroll
+        for (int r = 0; r < R; ++r) part[m][c][r] = __float2half2_rn(0.f);
+    int chain_steps = 0;
+
+    // warps whose columns all lie right of the image have nothing to compute
+    const bool any_col = ti.w0 + col0 < p.W;
+
+    // slot of row trow0 of this tile (row 0 of the tile is at rel_x)
+    int my_slot = rel_x.slot + trow0;
+    if (my_slot >= RR) my_slot -= RR;
+
+    // Rows [0, tile_h) are needed by step 0.
+    for (int q = 0; q < min(p.tile_h, ti.nrows) && ok; ++q) {
+      ok = mbar_wait_bounded(&full_x[wait_x.slot], wait_x.phase, p.err, 1);
+      wait_x.next(RR);
+    }
+
+    for (int st = 0; st < ti.nsteps && ok; ++st) {
+      if (st > 0 && st + p.tile_h - 1 < ti.nrows) {  // row st + tile_h - 1 arrives for this step
+        ok = mbar_wait_bounded(&full_x[wait_x.slot], wait_x.phase, p.err, 1);
+        wait_x.next(RR);
       }
-      *reinterpret_cast<__half2*>(p.y + off) = __floats2half2_rn(vx, vy);
+      if (ok) ok = mbar_wait_bounded(&full_w[wait_w.slot], wait_w.phase, p.err, 2);
+      if (!ok) break;
+
+      const int s = ti.s_lo + st;  // kernel row
+      const __half2* wrow = reinterpret_cast<const __half2*>(wring + wait_w.slot * wrow_bytes) + lane;
+      const int slot1 = (my_slot + 1 == RR) ? 0 : my_slot + 1;
+      const __half2* xrow0 = reinterpret_cast<const __half2*>(xring + my_slot * row_bytes) + xoff;
+      const __half2* xrow1 = reinterpret_cast<const __half2*>(xring + slot1 * row_bytes) + xoff;
+      const int out0 = ti.h0 + trow0;
+      const int in0 = out0 - PAD + s;
+      const bool v0 = any_col && out0 < p.H && in0 >= 0 && in0 < p.H;                        // warp-uniform
+      const bool v1 = any_col && M == 2 && out0 + 1 < p.H && in0 + 1 >= 0 && in0 + 1 < p.H;  // warp-uniform
+
+      if (v0 || v1) {
+        step_rows<K, R, M, ACC>(acc, part, wrow, xrow0, xrow1, v0, v1);
+      }
+      if constexpr (ACC == 1) {
+        if (++chain_steps == p.chain_rows || st + 1 == ti.nsteps) {  // the fp16 chains end here
+          chain_steps = 0;
+#pragma unroll
+          for (int m = 0; m < M; ++m)
+#pragma unroll
+            for (int c = 0; c < SPLIT; ++c)
+#pragma unroll
+              for (int r = 0; r < R; ++r) {
+                add_h2_to_f32x2(acc[m][r], part[m][c][r]);
+                part[m][c][r] = __float2half2_rn(0.f);
+              }
+        }
+      }
+
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&empty_x[rel_x.slot]);  // row st of the tile is never read again
+        mbar_arrive(&empty_w[wait_w.slot]);
+      }
+      rel_x.next(RR);
+      wait_w.next(RW);
+      my_slot = slot1;
+    }
+    if (!ok) break;
+    // The last tile_h - 1 rows of the tile are done too.
+    __syncwarp();
+    for (int q = ti.nsteps; q < ti.nrows; ++q) {
+      if (lane == 0) mbar_arrive(&empty_x[rel_x.slot]);
+      rel_x.next(RR);
+    }
+
+    // ---------------- fused epilogue ----------------
+    const int c = ti.c0 + 2 * lane;
+    if (c < p.C) {
+      if (c != bias_c0) {
+        bias_c0 = c;
+        if (p.bias) bias = __half22float2(*reinterpret_cast<const __half2*>(p.bias + c));
+        if (p.scale) scale = __half22float2(*reinterpret_cast<const __half2*>(p.scale + c));
+        if (p.shift) shift = __half22float2(*reinterpret_cast<const __half2*>(p.shift + c));
+      }
+      const int wlast = p.W - (ti.w0 + col0);  // columns r < wlast are inside the image
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        const int h = ti.h0 + trow0 + m;
+        if (h >= p.H) continue;
+        const long long row_off = ((static_cast<long long>(ti.b) * p.H + h) * p.W + (ti.w0 + col0)) * p.C + c;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          if (r >= wlast) break;
+          const long long off = row_off + static_cast<long long>(r) * p.C;
+          const float2 a = f32x2_unpack(acc[m][r]);
+          float vx = apply_act(a.x + bias.x, p.act) * scale.x + shift.x;
+          float vy = apply_act(a.y + bias.y, p.act) * scale.y + shift.y;
+          if (p.residual) {
+            const float2 res = __half22float2(*reinterpret_cast<const __half2*>(p.residual + off));
+            vx += res.x;
+            vy += res.y;
+          }
+          *reinterpret_cast<__half2*>(p.y + off) = __floats2half2_rn(vx, vy);
+        }
+      }
     }
   }
 }
@@ -269,8 +367,8 @@ struct KernelEntry {
   const void* fn;
 };
 
-// Variants compiled into this library for kernel size K (nullptr-terminated
-// by count).  Defined in dw_kernels_k*.cu.
+// Variants compiled into this library for kernel size K.  Defined in
+// dw_kernels_k*.cu.
 int kernels_for_k(int K, const KernelEntry** out);
 
 }  // namespace dwb

@@ -28,8 +28,20 @@ constexpr int kPixelBytes = 128;
 constexpr int kBarrierBytes = 1024;
 constexpr int kMaxConsumerWarps = 16;
 constexpr int kMaxBoxDim = 256;  // TMA box limit per dimension
+constexpr double kLoadLatency = 2000.0;  // clocks from TMA issue to data (L2/HBM), modelled
 
 inline long long ceil_div(long long a, long long b) { return (a + b - 1) / b; }
+
+// Registers are allocated per warp in units of 256, and a CTA's warps are
+// spread round-robin over the SM's 4 sub-partitions, each with a quarter of
+// the register file.  Returns how many CTAs of `warps` warps fit on one SM by
+// registers (0 = not even one).
+inline int ctas_by_registers(int regs_per_thread, int warps, int regs_per_sm) {
+  const long long per_warp = ceil_div(static_cast<long long>(regs_per_thread) * 32, 256) * 256;
+  const long long warps_per_smsp = (regs_per_sm / 4) / per_warp;  // warps one sub-partition can hold
+  const long long cta_warps_per_smsp = (warps + 3) / 4;            // a CTA's share of one sub-partition
+  return static_cast<int>(warps_per_smsp / cta_warps_per_smsp);    // conservative
+}
 
 // Valid kernel rows for output row h (input rows inside [0, H)).
 inline int valid_taps(int h, int H, int K) {
@@ -72,7 +84,6 @@ int enumerate_plans(const dwb_problem& pr, const HwInfo& hw, RegsFn regs, void* 
       const int M = kVariantM[mi];
       const int rg = regs ? regs(K, R, M, pr.accum, ctx) : estimate_regs(K, R, M, pr.accum);
       if (rg <= 0) continue;  // variant not compiled
-      const int regs_alloc = ((rg + 7) / 8) * 8;
       const int ncg_box = (kMaxBoxDim - (K - 1)) / R;
       const int ncg_need = static_cast<int>(ceil_div(std::min<long long>(W, 8LL * R), R));
       const int ncg_hi = std::min({8, ncg_box, ncg_need});
@@ -85,25 +96,17 @@ int enumerate_plans(const dwb_problem& pr, const HwInfo& hw, RegsFn regs, void* 
           if (tile_h > H + M - 1) break;  // taller tiles only add empty rows
           const int consumer_warps = nrg * ncg;
           const int threads = (consumer_warps + 1) * 32;
-          if (static_cast<long long>(threads) * regs_alloc > hw.regs_per_sm) break;
-          const int ring_rows = std::min(tile_h + 2, tile_h + K - 1);
-          const int ring_wrows = std::min(3, K);
-          const long long smem = kBarrierBytes + static_cast<long long>(ring_rows) * tile_w_in * kPixelBytes +
-                                 static_cast<long long>(ring_wrows) * K * kPixelBytes;
-          if (smem > hw.smem_optin) break;
-          const int cps = static_cast<int>(std::min<long long>(
-              {hw.smem_per_sm / (smem + hw.smem_reserved), hw.regs_per_sm / (static_cast<long long>(threads) * regs_alloc),
-               hw.max_threads_sm / threads, hw.max_ctas_sm}));
-          if (cps < 1) continue;
+          const int cps_regs = ctas_by_registers(rg, consumer_warps + 1, hw.regs_per_sm);
+          if (cps_regs < 1) break;
           const long long tiles_h = ceil_div(H, tile_h);
-          const long long grid = B * tiles_h * tiles_w * cblocks;
-          if (grid > 0x7fffffffLL) continue;
+          const long long tiles = B * tiles_h * tiles_w * cblocks;
+          if (tiles > (1LL << 40)) continue;
 
           // Work per CTA, averaged over the tile rows of the image.
           const double row_cost =
               pr.accum == DWB_ACCUM_F32 ? 2.0 * R * K + 4.0 * (R + K - 1) : 2.0 * R * K + 6.0 * R;
           const double wrow_cost = pr.accum == DWB_ACCUM_F32 ? 4.0 * K : 1.0 * K;
-          double work_sum = 0.0, bytes_sum = 0.0;
+          double work_sum = 0.0, bytes_sum = 0.0, steps_sum = 0.0;
           for (long long t = 0; t < tiles_h; ++t) {
             const int h0 = static_cast<int>(t * tile_h);
             const int rows_in = static_cast<int>(std::min<long long>(tile_h, H - h0));
@@ -115,17 +118,45 @@ int enumerate_plans(const dwb_problem& pr, const HwInfo& hw, RegsFn regs, void* 
             // per warp column group: every row group walks all steps
             work_sum += ncg * (valid * row_cost + static_cast<double>(nsteps) * nrg * wrow_cost);
             bytes_sum += (static_cast<double>(nsteps + tile_h - 1) * tile_w_in + nsteps * K) * kPixelBytes;
+            steps_sum += nsteps;
           }
           const double work_cta = work_sum / static_cast<double>(tiles_h);
           const double bytes_cta = bytes_sum / static_cast<double>(tiles_h);
-          const long long ctas_busiest = ceil_div(grid, hw.sm_count);
-          const long long resident = std::min<long long>(cps, ctas_busiest);
-          const double warps_per_smsp = static_cast<double>(resident * consumer_warps) / 4.0;
-          const double util = warps_per_smsp >= 2.0 ? 1.0 : (warps_per_smsp >= 1.0 ? 0.85 : 0.85 * warps_per_smsp);
-          const double t_compute = static_cast<double>(ctas_busiest) * work_cta / (4.0 * util);
-          const double t_load = static_cast<double>(ctas_busiest) * bytes_cta / 64.0;
-          const double waves = std::ceil(static_cast<double>(ctas_busiest) / static_cast<double>(cps));
-          const double cost = std::max(t_compute, t_load) + waves * 2000.0;
+          const double steps_cta = steps_sum / static_cast<double>(tiles_h);
+          const long long tiles_busiest = ceil_div(tiles, hw.sm_count);  // tiles on the busiest SM
+
+          // Prefetch depth (rows the producer may run ahead of the consumers):
+          // deeper rings hide the load latency, shallower ones fit more CTAs.
+          int last_ring = -1;
+          const int depths[4] = {2, 4, 8, K + 64};
+          for (int di = 0; di < 4; ++di) {
+            const int ring_rows = std::min(tile_h + depths[di], tile_h + K - 1);
+            if (ring_rows == last_ring) continue;
+            last_ring = ring_rows;
+            const int ring_wrows = std::min(std::max(3, depths[di] + 1), K);
+            const long long smem = kBarrierBytes + static_cast<long long>(ring_rows) * tile_w_in * kPixelBytes +
+                                   static_cast<long long>(ring_wrows) * K * kPixelBytes;
+            if (smem > hw.smem_optin) break;
+            if (2 * (ring_rows + ring_wrows) * 8 > kBarrierBytes) break;
+            const int cps = static_cast<int>(std::min<long long>(
+                {hw.smem_per_sm / (smem + hw.smem_reserved), static_cast<long long>(cps_regs),
+                 hw.max_threads_sm / threads, hw.max_ctas_sm}));
+            if (cps < 1) continue;
+            const long long grid = std::min<long long>(tiles, static_cast<long long>(cps) * hw.sm_count);
+            const long long resident = std::min<long long>(cps, tiles_busiest);
+            const double warps_per_smsp = static_cast<double>(resident * consumer_warps) / 4.0;
+            const double util = warps_per_smsp >= 3.0   ? 1.0
+                                : warps_per_smsp >= 2.0 ? 0.9
+                                : warps_per_smsp >= 1.0 ? 0.65
+                                                        : 0.65 * warps_per_smsp;
+            const double t_tp = std::max(static_cast<double>(tiles_busiest) * work_cta / (4.0 * util),
+                                         static_cast<double>(tiles_busiest) * bytes_cta / 64.0);
+            // a persistent CTA pays the load latency once, then once per step it
+            // cannot prefetch far enough ahead
+            const double tiles_per_cta = std::ceil(static_cast<double>(tiles) / static_cast<double>(grid));
+            const double ahead = static_cast<double>(ring_rows - tile_h + 1);  // steps of lookahead
+            const double t_lat = kLoadLatency + tiles_per_cta * (steps_cta * kLoadLatency / ahead + 300.0);
+            const double cost = std::max(t_tp, t_lat) + tiles_per_cta * 300.0;
           dwb_plan pl;
           std::memset(&pl, 0, sizeof(pl));
           pl.kernel_size = K;
@@ -142,11 +173,13 @@ int enumerate_plans(const dwb_problem& pr, const HwInfo& hw, RegsFn regs, void* 
           pl.smem_bytes = static_cast<int32_t>(smem);
           pl.ctas_per_sm = cps;
           pl.grid = grid;
+          pl.tiles = tiles;
           pl.accum = pr.accum;
           pl.regs_estimate = rg;
           pl.model_cost = cost;
           ++count;
           if (sink) sink(pl, sink_ctx);
+          }
         }
       }
     }
@@ -201,10 +234,14 @@ int check_plan(const dwb_problem& pr, const HwInfo& hw, int regs, dwb_plan* p) {
   const long long smem = kBarrierBytes + static_cast<long long>(p->ring_rows) * p->tile_w_in * kPixelBytes +
                          static_cast<long long>(p->ring_wrows) * K * kPixelBytes;
   if (smem > hw.smem_optin) return DWB_ERR_BAD_ARG;
-  if (regs > 0 && static_cast<long long>(p->threads) * ((regs + 7) / 8 * 8) > hw.regs_per_sm) return DWB_ERR_BAD_ARG;
+  if (regs > 0 && ctas_by_registers(regs, cw + 1, hw.regs_per_sm) < 1) return DWB_ERR_BAD_ARG;
   p->smem_bytes = static_cast<int32_t>(smem);
-  p->grid = pr.batch * ceil_div(pr.height, p->tile_h) * ceil_div(pr.width, p->tile_w) *
-            ceil_div(pr.channels, kChannelsPerCta);
+  p->tiles = pr.batch * ceil_div(pr.height, p->tile_h) * ceil_div(pr.width, p->tile_w) *
+             ceil_div(pr.channels, kChannelsPerCta);
+  if (p->tiles > (1LL << 40)) return DWB_ERR_BAD_SHAPE;
+  // grid: < 0 = persistent (sized by the launcher from the occupancy), else
+  // the caller's CTA count, at most one per tile (0 = one CTA per tile)
+  if (p->grid == 0 || p->grid > p->tiles) p->grid = p->tiles;
   if (p->grid > 0x7fffffffLL) return DWB_ERR_BAD_SHAPE;
   p->regs_estimate = regs;
   return DWB_OK;

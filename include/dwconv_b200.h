@@ -84,7 +84,8 @@ typedef struct dwb_plan {
     int32_t threads;
     int32_t smem_bytes;
     int32_t ctas_per_sm;
-    int64_t grid;               /* CTAs launched                                */
+    int64_t grid;               /* CTAs launched (persistent: <= tiles)         */
+    int64_t tiles;              /* output tiles, walked by the CTAs in strides  */
     int32_t accum;              /* dwb_accum actually used                      */
     int32_t regs_estimate;      /* registers/thread assumed by the planner      */
     double model_cost;          /* planner's modelled time (arbitrary units)     */

@@ -103,11 +103,14 @@ def test_plans_respect_hardware_limits(B, H, W, C, K, accum):
     assert p["tile_w_in"] == p["tile_w"] + K - 1 <= 256                 # TMA box limit
     assert p["consumer_warps"] == (p["tile_w"] // R) * (p["tile_h"] // M)
     assert p["threads"] == 32 * (p["consumer_warps"] + 1) <= 1024
-    assert p["threads"] * ((p["regs_estimate"] + 7) // 8 * 8) <= 65536
+    # registers: per warp in units of 256, a CTA's warps spread over 4 sub-partitions of 16K each
+    per_warp = -(-p["regs_estimate"] * 32 // 256) * 256
+    assert -(-(p["consumer_warps"] + 1) // 4) * per_warp <= 16384
     assert p["smem_bytes"] <= 232448 and p["ctas_per_sm"] >= 1
     assert p["ring_rows"] >= p["tile_h"] and p["ring_wrows"] >= 1
     tiles = -(-H // p["tile_h"]) * -(-W // p["tile_w"]) * -(-C // 64)
-    assert p["grid"] == B * tiles
+    assert p["tiles"] == B * tiles
+    assert 1 <= p["grid"] <= min(p["tiles"], p["ctas_per_sm"] * 148) or (B == 0 and p["grid"] == 0)
 
 
 def test_plan_rejects_bad_problems():
