@@ -55,6 +55,13 @@ def parse_args():
     ap.add_argument("--batch", type=int, default=1, help="images per GPU per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
+    ap.add_argument("--workload", choices=["convmixer", "dw"], default="convmixer",
+                    help="convmixer: the headline ConvMixer-1536/20 img/s; dw: one depthwise layer (µs/layer)")
+    ap.add_argument("--shape", default="64,56,56,1024,31",
+                    help="dw workload: global B,H,W,C,K (the batch is sharded over the ranks)")
+    ap.add_argument("--epilogue", choices=["none", "gelu_bn"], default="gelu_bn",
+                    help="dw workload: plain conv, or the fused bias+GELU+BN-scale/shift epilogue")
+    ap.add_argument("--accum", choices=["mixed", "f32"], default="mixed")
     return ap.parse_args()
 
 
@@ -152,7 +159,7 @@ def measured_peaks():
 
 def profiled_traffic():
     """DRAM bytes per launch of the DW kernel from the committed ncu summary, if present."""
-    path = os.path.join(ROOT, "profiles", "dw_traffic.json")
+    path = os.path.join(ROOT, "profiles", "dw_traffic.txt")
     try:
         with open(path) as f:
             return json.load(f)
@@ -343,6 +350,99 @@ def run_ours(args):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------- one depthwise layer
+
+def run_dw(args):
+    """µs/layer of one depthwise layer (BASELINE configs[2..4]); the batch is sharded over the ranks."""
+    import torch
+    import torch.distributed as dist
+
+    import depthwise_conv_b200 as dwb
+    from depthwise_conv_b200 import _lib
+    from depthwise_conv_b200.shard import max_over_ranks, shard_range
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    Bg, H, W, C, K = (int(v) for v in args.shape.split(","))
+    lo, hi = shard_range(Bg, world, rank)
+    B = hi - lo
+    accum = _lib.ACCUM_MIXED if args.accum == "mixed" else _lib.ACCUM_F32
+    gen = torch.Generator().manual_seed(0)
+    # seeded per image so every GPU count sees the same data: x ~ N(0,1), w ~ N(0, 1/K^2)
+    x = torch.randn(Bg, C, H, W, generator=gen)[lo:hi].half().to(dev).contiguous(memory_format=torch.channels_last)
+    w = (torch.randn(K, K, C, generator=gen) / K).half().to(dev)
+    epi = args.epilogue == "gelu_bn"
+    bias = torch.zeros(C, dtype=torch.float16, device=dev) if epi else None
+    scale = torch.full((C,), 1.0 / (1.0 + 1e-5) ** 0.5, dtype=torch.float16, device=dev) if epi else None
+    shift = torch.zeros(C, dtype=torch.float16, device=dev) if epi else None
+    act = "gelu" if epi else "none"
+    y = torch.empty_like(x)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(dev)
+    layer = lambda: dwb.conv2d_nhwc_fused(x, w, bias, scale, shift, None, act, accum, out=y)  # noqa: E731
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            if B:
+                layer()
+        stream.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    clocks.start()
+    with torch.cuda.stream(stream):
+        for i in range(args.steps):
+            flush.add_(1.0)  # L2 flush between timed iterations
+            evs[i][0].record(stream)
+            if B:
+                layer()
+            evs[i][1].record(stream)
+        stream.synchronize()
+    clk = clocks.stop()
+    ms = sum(s.elapsed_time(e) for s, e in evs)
+    if world > 1:
+        dist.barrier()
+    ms_max = max_over_ranks(ms, dev)
+    us_layer = ms_max * 1000.0 / args.steps
+    hfma2_tf, ffma2_tf = dwb.probe_fma_peak(stream.cuda_stream)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    fl = valid_flops(Bg, H, W, C, K)
+    by = dw_bytes(Bg, H, W, C, K, epilogue=False) + (3 * 2 * C if epi else 0)
+    achieved = fl / (us_layer * 1e-6) / 1e12
+    peaks = measured_peaks()
+    plan = _lib.plan_query(max(1, -(-Bg // world)), H, W, C, K, accum)
+    line = {
+        "metric": "DW-conv µs/layer", "value": us_layer, "unit": "us/layer", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": us_layer / 1000.0, "higher_is_better": False,
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "fp16 (" + ("fp16x2 FMA chains, fp32 accumulation" if accum else "fp32 FMA") + ")",
+        "data": "synthetic x ~ N(0,1), w ~ N(0,1/k^2), seeded",
+        "config": {"workload": "depthwise layer", "B": Bg, "H": H, "W": W, "C": C, "K": K,
+                   "epilogue": args.epilogue, "images_per_s": Bg / (us_layer * 1e-6),
+                   "parallelism": f"batch-sharded x{world}, no collectives",
+                   "l2": "flushed (256 MB write) between timed iterations",
+                   "plan": {k: plan[k] for k in ("cols_per_thread", "rows_per_thread", "tile_h", "tile_w",
+                                                 "consumer_warps", "accum")}},
+        "roofline": {"bound": "fma", "achieved": achieved, "peak": hfma2_tf, "unit": "TFLOP/s",
+                     "frac": achieved / hfma2_tf, "flops_per_launch": fl,
+                     "traffic": profiled_traffic().get(f"dw_{Bg}_{H}_{W}_{C}_{K}"),
+                     "peak_source": "measured in this run: CUDA-core HFMA2 microbenchmark",
+                     "hbm": {"achieved": by / (us_layer * 1e-6) / 1e9, "peak": peaks.get("hbm_gbs"), "unit": "GB/s",
+                             "bytes_per_launch": by}},
+        "gpu_launches": args.steps,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 # ----------------------------------------------------------------------------- reference arm
 
 def run_reference(args):
@@ -381,9 +481,10 @@ def run_reference(args):
 def main():
     args = parse_args()
     if args.impl == "reference":
-        if args.steps > 10:  # each CPU step is ~1 s; keep the run within minutes
-            args.steps = 10
+        args.warmup = min(args.warmup, 2)  # each CPU step is one image (~0.1 s on the GPU hosts)
         run_reference(args)
+    elif args.workload == "dw":
+        run_dw(args)
     else:
         run_ours(args)
 

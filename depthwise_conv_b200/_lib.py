@@ -28,6 +28,7 @@ ERR_BAD_ARG = 8
 ACT_NONE, ACT_RELU, ACT_GELU = 0, 1, 2
 ACT_CODES = {"none": ACT_NONE, "relu": ACT_RELU, "gelu": ACT_GELU}
 ACCUM_F32, ACCUM_MIXED = 0, 1
+ACCUM_DEFAULT = ACCUM_MIXED  # DWB_ACCUM_DEFAULT
 
 # Every entry point the header declares, with its ctypes signature.
 _p, _i, _i64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
@@ -138,7 +139,7 @@ def call(fn: str, *args) -> None:
     check(fn, getattr(load(), fn)(*args))
 
 
-def plan_query(B: int, H: int, W: int, C: int, K: int, accum: int = ACCUM_F32, sm_count: int = 0,
+def plan_query(B: int, H: int, W: int, C: int, K: int, accum: int = ACCUM_DEFAULT, sm_count: int = 0,
                smem_optin: int = 0) -> dict:
     """The planner's choice for a problem (host arithmetic only, no GPU needed)."""
     pr = Problem(B, H, W, C, K, accum)
@@ -147,7 +148,7 @@ def plan_query(B: int, H: int, W: int, C: int, K: int, accum: int = ACCUM_F32, s
     return out.as_dict()
 
 
-def plan_candidates(B: int, H: int, W: int, C: int, K: int, accum: int = ACCUM_F32, sm_count: int = 0,
+def plan_candidates(B: int, H: int, W: int, C: int, K: int, accum: int = ACCUM_DEFAULT, sm_count: int = 0,
                     smem_optin: int = 0) -> list[dict]:
     """Every feasible plan of a problem with its modelled cost (host arithmetic only)."""
     pr = Problem(B, H, W, C, K, accum)

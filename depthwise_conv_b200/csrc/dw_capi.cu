@@ -69,7 +69,7 @@ static const KernelEntry* find_variant(int K, int R, int M, int acc) {
 static __device__ int g_device_error;
 
 constexpr int kMaxDevices = 64;
-constexpr int kMaxVariants = 16 * 16;  // K values x variants per K
+constexpr int kMaxVariants = 16 * kNumVariantR * 4;  // K values x R x M x accum
 
 struct VariantState {
   int regs = -1;         // -1 unknown, 0 unavailable
@@ -108,10 +108,10 @@ static DeviceState g_devices[kMaxDevices];
 
 static int variant_slot(int K, int R, int M, int acc) {
   int ri = 0;
-  for (; ri < 4; ++ri)
+  for (; ri < kNumVariantR - 1; ++ri)
     if (kVariantR[ri] == R) break;
   const int mi = (M == 2) ? 0 : 1;
-  return ((K / 2) * 16) + (ri * 4) + (mi * 2) + acc;
+  return ((K / 2) * kNumVariantR + ri) * 4 + mi * 2 + acc;
 }
 
 static void init_device(int dev, DeviceState* st) {
@@ -231,12 +231,11 @@ static inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cas
 
 // Mixed accumulation: kernel rows per fp16 chain.  A chain of L fp16
 // roundings leaves a relative error of about 2e-4 * sqrt(L / 2) (random
-// walk of half-ulp roundings); chains stay at <= 24 taps (K >= 25 rows are
-// split in two by the kernel itself).
+// walk of half-ulp roundings); chains cover one kernel row (K >= 25 rows are
+// split in two by the kernel itself), so L <= 16.
 static int mixed_chain_rows(int K) {
-  if (K >= 25) return 1;
-  const int rows = 24 / K;
-  return rows > 3 ? 3 : rows;
+  (void)K;
+  return 1;  // one kernel row per chain: the partials stay step-local (fewer registers)
 }
 
 // Argument checks shared by every entry point (no CUDA calls).  An empty
@@ -459,7 +458,7 @@ int dwb_conv2d_nhwc_fwd_planned(const void* x, const void* w, const void* bias, 
 
 int dwb_conv2d_nhwc_fwd(const void* x, const void* w, void* y, int64_t B, int64_t H, int64_t W, int64_t C, int K,
                         void* stream) {
-  return launch_forward(x, w, nullptr, nullptr, nullptr, nullptr, y, B, H, W, C, K, DWB_ACT_NONE, DWB_ACCUM_F32,
+  return launch_forward(x, w, nullptr, nullptr, nullptr, nullptr, y, B, H, W, C, K, DWB_ACT_NONE, DWB_ACCUM_DEFAULT,
                         stream);
 }
 
@@ -474,7 +473,7 @@ int dwb_depthwise_forward_32_768_7(const void* input, const void* weight, void* 
   int rc = fixed_shape(tensorHeight, tensorWidth, Ch, windowSize, 32, 32, 768, 7);
   if (rc != DWB_OK) return rc;
   return launch_forward(input, weight, nullptr, nullptr, nullptr, nullptr, output, B, 32, 32, 768, 7, DWB_ACT_NONE,
-                        DWB_ACCUM_F32, stream);
+                        DWB_ACCUM_DEFAULT, stream);
 }
 
 static int forward_32_1536_9(const void* input, const void* weight, void* output, int tensorHeight, int tensorWidth,
@@ -483,7 +482,7 @@ static int forward_32_1536_9(const void* input, const void* weight, void* output
   if (rc != DWB_OK) return rc;
   if (batchStride != 32 * 32 * 1536) return DWB_ERR_BAD_SHAPE;  // images are packed NHWC
   return launch_forward(input, weight, nullptr, nullptr, nullptr, nullptr, output, B, 32, 32, 1536, 9, DWB_ACT_NONE,
-                        DWB_ACCUM_F32, stream);
+                        DWB_ACCUM_DEFAULT, stream);
 }
 
 int dwb_depthwise_forward_32_1536_9(const void* input, const void* weight, void* output, int tensorHeight,
@@ -502,7 +501,7 @@ int dwb_depthwise_forward_16_1536_9(const void* input, const void* weight, void*
   int rc = fixed_shape(tensorHeight, tensorWidth, Ch, windowSize, 16, 16, 1536, 9);
   if (rc != DWB_OK) return rc;
   return launch_forward(input, weight, nullptr, nullptr, nullptr, nullptr, output, B, 16, 16, 1536, 9, DWB_ACT_NONE,
-                        DWB_ACCUM_F32, stream);
+                        DWB_ACCUM_DEFAULT, stream);
 }
 
 int dwb_depthwise_forward_32_1536_13(const void* input, const void* weight, void* output, int tensorHeight,
@@ -510,14 +509,14 @@ int dwb_depthwise_forward_32_1536_13(const void* input, const void* weight, void
   int rc = fixed_shape(tensorHeight, tensorWidth, Ch, windowSize, 32, 32, 1536, 13);
   if (rc != DWB_OK) return rc;
   return launch_forward(input, weight, nullptr, nullptr, nullptr, nullptr, output, B, 32, 32, 1536, 13,
-                        DWB_ACT_NONE, DWB_ACCUM_F32, stream);
+                        DWB_ACT_NONE, DWB_ACCUM_DEFAULT, stream);
 }
 
 static int replknet_forward(const void* input, const void* weight, const void* bias, void* output, int B, int C,
                             int H, int W, int eC, int eHW, int eK, void* stream) {
   if (C != eC || H != eHW || W != eHW) return DWB_ERR_BAD_SHAPE;
   return launch_forward(input, weight, bias, nullptr, nullptr, nullptr, output, B, H, W, C, eK, DWB_ACT_NONE,
-                        DWB_ACCUM_F32, stream);
+                        DWB_ACCUM_DEFAULT, stream);
 }
 
 int dwb_depthwise_31x31_128_nhwc(const void* input, const void* weight, const void* bias, void* output, int B, int C,

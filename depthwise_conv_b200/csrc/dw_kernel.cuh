@@ -152,11 +152,43 @@ __device__ __forceinline__ void step_rows(f32x2 (&acc)[M][R], __half2 (&part)[M]
   }
 }
 
+// Epilogue of one warp slot: y = act(acc) * scale + shift (+ residual), where
+// the accumulators already started from the bias.  ACT / RES are resolved
+// once per tile by the caller, so the loop is straight-line code.
+template <int ACT, bool RES, int M, int R>
+__device__ __forceinline__ void store_slot(const f32x2 (&acc)[M][R], f32x2 scale, f32x2 shift, __half2* y,
+                                           const __half2* res, long long row_h2, int col_h2, int rows_valid,
+                                           int cols_valid) {
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+    if (m >= rows_valid) break;
+    __half2* yp = y + m * row_h2;
+    const __half2* rp = RES ? res + m * row_h2 : nullptr;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if (r >= cols_valid) break;
+      float2 a = f32x2_unpack(acc[m][r]);
+      if (ACT != kActNone) {
+        a.x = apply_act(a.x, ACT);
+        a.y = apply_act(a.y, ACT);
+      }
+      f32x2 v = shift;
+      ffma2(v, f2_bits(a), scale);  // a * scale + shift, both channels in one FFMA2
+      float2 o = f32x2_unpack(v);
+      if (RES) {
+        const float2 rv = __half22float2(rp[r * col_h2]);
+        o.x += rv.x;
+        o.y += rv.y;
+      }
+      yp[r * col_h2] = __floats2half2_rn(o.x, o.y);
+    }
+  }
+}
+
 template <int K, int R, int M, int ACC>
 __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                  const __grid_constant__ CUtensorMap tmap_w, const DwParams p) {
   constexpr int PAD = K / 2;
-  constexpr int NJ = R + K - 1;  // input columns a thread slides over
   constexpr int SPLIT = (ACC == 1 && K >= 25) ? 2 : 1;
   extern __shared__ __align__(1024) unsigned char smem[];
 
@@ -241,17 +273,32 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
   RingPos rel_x;   // next input row to release
   bool ok = true;
 
-  float2 bias = make_float2(0.f, 0.f), scale = make_float2(1.f, 1.f), shift = make_float2(0.f, 0.f);
+  f32x2 bias = 0, scale = 0, shift = 0;
   int bias_c0 = -1;
 
   for (uint32_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
     const TileInfo ti = decode_tile<K>(p, t);
 
-    f32x2 acc[M][R];  // packed fp32 (channel 2l, channel 2l+1)
+    // per-channel epilogue parameters, reloaded when the tile's channels change
+    if (ti.c0 != bias_c0) {
+      bias_c0 = ti.c0;
+      const int c = ti.c0 + 2 * lane;
+      float2 b = make_float2(0.f, 0.f), sc = make_float2(1.f, 1.f), sh = make_float2(0.f, 0.f);
+      if (c < p.C) {
+        if (p.bias) b = __half22float2(*reinterpret_cast<const __half2*>(p.bias + c));
+        if (p.scale) sc = __half22float2(*reinterpret_cast<const __half2*>(p.scale + c));
+        if (p.shift) sh = __half22float2(*reinterpret_cast<const __half2*>(p.shift + c));
+      }
+      bias = f2_bits(b);
+      scale = f2_bits(sc);
+      shift = f2_bits(sh);
+    }
+
+    f32x2 acc[M][R];  // packed fp32 (channel 2l, channel 2l+1), starting from the bias
 #pragma unroll
     for (int m = 0; m < M; ++m)
 #pragma unroll
-      for (int r = 0; r < R; ++r) acc[m][r] = f32x2_zero();
+      for (int r = 0; r < R; ++r) acc[m][r] = bias;
     __half2 part[M][SPLIT][R];  // mixed mode fp16 chains (unused in fp32 mode)
 #pragma unroll
     for (int m = 0; m < M; ++m)
@@ -329,33 +376,21 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
 
     // ---------------- fused epilogue ----------------
     const int c = ti.c0 + 2 * lane;
-    if (c < p.C) {
-      if (c != bias_c0) {
-        bias_c0 = c;
-        if (p.bias) bias = __half22float2(*reinterpret_cast<const __half2*>(p.bias + c));
-        if (p.scale) scale = __half22float2(*reinterpret_cast<const __half2*>(p.scale + c));
-        if (p.shift) shift = __half22float2(*reinterpret_cast<const __half2*>(p.shift + c));
-      }
-      const int wlast = p.W - (ti.w0 + col0);  // columns r < wlast are inside the image
-#pragma unroll
-      for (int m = 0; m < M; ++m) {
-        const int h = ti.h0 + trow0 + m;
-        if (h >= p.H) continue;
-        const long long row_off = ((static_cast<long long>(ti.b) * p.H + h) * p.W + (ti.w0 + col0)) * p.C + c;
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-          if (r >= wlast) break;
-          const long long off = row_off + static_cast<long long>(r) * p.C;
-          const float2 a = f32x2_unpack(acc[m][r]);
-          float vx = apply_act(a.x + bias.x, p.act) * scale.x + shift.x;
-          float vy = apply_act(a.y + bias.y, p.act) * scale.y + shift.y;
-          if (p.residual) {
-            const float2 res = __half22float2(*reinterpret_cast<const __half2*>(p.residual + off));
-            vx += res.x;
-            vy += res.y;
-          }
-          *reinterpret_cast<__half2*>(p.y + off) = __floats2half2_rn(vx, vy);
-        }
+    const int rows_valid = min(M, p.H - (ti.h0 + trow0));
+    const int cols_valid = min(R, p.W - (ti.w0 + col0));
+    if (c < p.C && rows_valid > 0 && cols_valid > 0) {
+      const long long base = ((static_cast<long long>(ti.b) * p.H + ti.h0 + trow0) * p.W + ti.w0 + col0) * p.C + c;
+      __half2* y = reinterpret_cast<__half2*>(p.y + base);
+      const __half2* res = p.residual ? reinterpret_cast<const __half2*>(p.residual + base) : nullptr;
+      const long long row_h2 = static_cast<long long>(p.W) * p.C / 2;
+      const int col_h2 = p.C / 2;
+      switch (p.act * 2 + (res != nullptr)) {  // one branch per tile, then straight-line stores
+        case 0: store_slot<kActNone, false>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
+        case 1: store_slot<kActNone, true>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
+        case 2: store_slot<kActRelu, false>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
+        case 3: store_slot<kActRelu, true>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
+        case 4: store_slot<kActGelu, false>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
+        default: store_slot<kActGelu, true>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
       }
     }
   }

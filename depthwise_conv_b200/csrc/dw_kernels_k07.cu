@@ -1,3 +1,3 @@
 // Compiled variants of the depthwise kernel for K = 7 (see dw_variants.cuh).
 #include "dw_variants.cuh"
-DWB_DEFINE_TABLE(7)
+DWB_DEFINE_TABLE_WIDE(7)

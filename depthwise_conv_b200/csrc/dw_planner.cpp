@@ -19,7 +19,14 @@
 
 namespace dwb {
 
-const int kVariantR[4] = {16, 14, 8, 7};
+const int kVariantR[kNumVariantR] = {32, 28, 16, 14, 8, 7};
+
+bool variant_compiled(int K, int R, int M, int acc) {
+  (void)acc;
+  if (M != 1 && M != 2) return false;
+  if (R == 7 || R == 8 || R == 14 || R == 16) return true;
+  return (R == 28 || R == 32) && K <= 13;
+}
 const int kVariantM[2] = {2, 1};
 
 namespace {
@@ -51,11 +58,11 @@ inline int valid_taps(int h, int H, int K) {
 }  // namespace
 
 int estimate_regs(int K, int R, int M, int acc) {
-  // accumulators (2 per output) + weights + addressing/temporaries
+  // accumulators (2 per output) + weights + fp16 chain partials + addressing
   const int w = acc == 0 ? 2 * K : K;
-  const int part = acc == 0 ? 0 : R;
-  int est = 2 * M * R + (M == 1 ? w / 2 : w) + part + 24;
-  return std::min(255, std::max(40, est));
+  const int part = acc == 0 ? 0 : (K >= 25 ? 2 * R : R);
+  int est = 2 * M * R + w + part + 28;
+  return std::min(255, std::max(48, est));
 }
 
 int validate_problem(const dwb_problem& pr) {
@@ -78,10 +85,11 @@ int enumerate_plans(const dwb_problem& pr, const HwInfo& hw, RegsFn regs, void* 
   const int pad = K / 2;
   int count = 0;
 
-  for (int ri = 0; ri < 4; ++ri) {
+  for (int ri = 0; ri < kNumVariantR; ++ri) {
     const int R = kVariantR[ri];
     for (int mi = 0; mi < 2; ++mi) {
       const int M = kVariantM[mi];
+      if (!variant_compiled(K, R, M, pr.accum)) continue;
       const int rg = regs ? regs(K, R, M, pr.accum, ctx) : estimate_regs(K, R, M, pr.accum);
       if (rg <= 0) continue;  // variant not compiled
       const int ncg_box = (kMaxBoxDim - (K - 1)) / R;
@@ -219,9 +227,7 @@ int check_plan(const dwb_problem& pr, const HwInfo& hw, int regs, dwb_plan* p) {
   if (vst != DWB_OK) return vst;
   const int K = pr.kernel_size;
   const int R = p->cols_per_thread, M = p->rows_per_thread;
-  bool known_r = false;
-  for (int r : kVariantR) known_r |= (r == R);
-  if (!known_r || (M != 1 && M != 2) || p->kernel_size != K || p->accum != pr.accum) return DWB_ERR_BAD_ARG;
+  if (!variant_compiled(K, R, M, p->accum) || p->kernel_size != K || p->accum != pr.accum) return DWB_ERR_BAD_ARG;
   if (p->tile_w < R || p->tile_w % R != 0 || p->tile_h < M || p->tile_h % M != 0) return DWB_ERR_BAD_ARG;
   if (p->tile_w + K - 1 > kMaxBoxDim) return DWB_ERR_BAD_ARG;
   const int cw = (p->tile_w / R) * (p->tile_h / M);

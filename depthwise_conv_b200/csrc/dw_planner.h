@@ -29,8 +29,10 @@ typedef int (*RegsFn)(int K, int R, int M, int acc, void* ctx);
 int estimate_regs(int K, int R, int M, int acc);
 
 // Column-group sizes and row blockings the library compiles (dw_variants.cuh).
-extern const int kVariantR[4];
+constexpr int kNumVariantR = 6;
+extern const int kVariantR[kNumVariantR];
 extern const int kVariantM[2];
+bool variant_compiled(int K, int R, int M, int acc);
 
 // Range checks shared by every entry point.  Returns a dwb_status.
 int validate_problem(const dwb_problem& pr);

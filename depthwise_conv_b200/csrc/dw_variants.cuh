@@ -1,7 +1,9 @@
 // dw_variants.cuh -- the (R, M, ACC) variants compiled for every kernel size.
 //   R (columns per thread) in {7, 8, 14, 16} covers the widths 7, 14, 16, 28,
-//   32 and 56 without overhang; M (rows per thread) in {1, 2}; ACC 0 = fp32
-//   FFMA2, 1 = fp16x2 row partials with fp32 accumulation across rows.
+//   32 and 56 without overhang, plus R in {28, 32} for K <= 13, where a wider
+//   register block amortises the per-kernel-row overhead over more FMAs;
+//   M (rows per thread) in {1, 2}; ACC 0 = fp32 FFMA2, 1 = fp16x2 chains with
+//   fp32 accumulation.  dw_planner.cpp (variant_compiled) mirrors this list.
 #pragma once
 #include "dw_kernel.cuh"
 
@@ -9,10 +11,15 @@
 #define DWB_VARIANTS_ACC(K, A)                                                                      \
   DWB_ENTRY(K, 7, 1, A), DWB_ENTRY(K, 7, 2, A), DWB_ENTRY(K, 8, 1, A), DWB_ENTRY(K, 8, 2, A),     \
       DWB_ENTRY(K, 14, 1, A), DWB_ENTRY(K, 14, 2, A), DWB_ENTRY(K, 16, 1, A), DWB_ENTRY(K, 16, 2, A)
+#define DWB_WIDE_ACC(K, A) \
+  DWB_ENTRY(K, 28, 1, A), DWB_ENTRY(K, 28, 2, A), DWB_ENTRY(K, 32, 1, A), DWB_ENTRY(K, 32, 2, A)
 #define DWB_VARIANTS(K) DWB_VARIANTS_ACC(K, 0), DWB_VARIANTS_ACC(K, 1)
+#define DWB_VARIANTS_WIDE(K) DWB_VARIANTS(K), DWB_WIDE_ACC(K, 0), DWB_WIDE_ACC(K, 1)
 
-#define DWB_DEFINE_TABLE(K)                                                          \
-  namespace dwb {                                                                    \
-  extern const KernelEntry kTableK##K[] = {DWB_VARIANTS(K)};                         \
+#define DWB_DEFINE_TABLE_OF(K, LIST)                                                      \
+  namespace dwb {                                                                         \
+  extern const KernelEntry kTableK##K[] = {LIST(K)};                                      \
   extern const int kCountK##K = static_cast<int>(sizeof(kTableK##K) / sizeof(KernelEntry)); \
   }
+#define DWB_DEFINE_TABLE(K) DWB_DEFINE_TABLE_OF(K, DWB_VARIANTS)
+#define DWB_DEFINE_TABLE_WIDE(K) DWB_DEFINE_TABLE_OF(K, DWB_VARIANTS_WIDE)

@@ -49,7 +49,7 @@ def _replknet_op(fn: str, input, weight, bias, C: int, HW: int, K: int):
                       torch.cuda.current_stream(input.device).cuda_stream)
         else:
             _lib.call("dwb_conv2d_nhwc_fused_fwd", input.data_ptr(), weight.data_ptr(), bp or None, None, None,
-                      None, output.data_ptr(), B, Hi, Wi, Ci, K, _lib.ACT_NONE, _lib.ACCUM_F32,
+                      None, output.data_ptr(), B, Hi, Wi, Ci, K, _lib.ACT_NONE, _lib.ACCUM_DEFAULT,
                       torch.cuda.current_stream(input.device).cuda_stream)
     return output
 

@@ -78,11 +78,13 @@ class _DeviceGuard:
 
 
 def conv2d_nhwc_fused(x: torch.Tensor, w: torch.Tensor, bias=None, scale=None, shift=None, residual=None,
-                      act: int | str = 0, accum: int = _lib.ACCUM_F32, out: torch.Tensor | None = None,
+                      act: int | str = 0, accum: int = _lib.ACCUM_DEFAULT, out: torch.Tensor | None = None,
                       plan: dict | None = None):
     """y = act(conv(x, w) + bias) * scale + shift + residual (each term optional).
 
     x: channels_last [B, C, H, W] fp16; w: [K, K, C] fp16.  Returns y like x.
+    ``accum``: ``_lib.ACCUM_MIXED`` (default; fp16x2 FMA chains of at most 24
+    taps added into fp32 accumulators) or ``_lib.ACCUM_F32`` (every tap in fp32).
     ``plan``: an explicit launch plan (a dict from ``plan_candidates``) instead
     of the planner's choice -- for autotuning.
     """

@@ -59,9 +59,13 @@ typedef enum dwb_act {
 } dwb_act;
 
 typedef enum dwb_accum {
-    DWB_ACCUM_F32 = 0,          /* fp32 accumulation of every tap (default)      */
-    DWB_ACCUM_MIXED = 1         /* fp16x2 per kernel row, fp32 across rows       */
+    DWB_ACCUM_F32 = 0,          /* every tap accumulated in fp32 (FFMA2)          */
+    DWB_ACCUM_MIXED = 1         /* fp16x2 HFMA2 chains of <= 24 taps, added into
+                                   fp32 accumulators (rel-L2 ~6e-4 vs exact)      */
 } dwb_accum;
+
+/* Accumulation used by the entry points that take no `accum` argument. */
+#define DWB_ACCUM_DEFAULT DWB_ACCUM_MIXED
 
 /* Problem description used by the planner. */
 typedef struct dwb_problem {
@@ -114,7 +118,7 @@ DWB_API const char* dwb_last_error(void);
 
 /* ---- generic entry points ------------------------------------------------ */
 
-/* y = conv(x, w): the plain depthwise convolution (no bias). */
+/* y = conv(x, w): the plain depthwise convolution (no bias), DWB_ACCUM_DEFAULT. */
 DWB_API int dwb_conv2d_nhwc_fwd(const void* x, const void* w, void* y,
                         int64_t B, int64_t H, int64_t W, int64_t C, int K,
                         void* stream);

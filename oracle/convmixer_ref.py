@@ -54,14 +54,19 @@ class ConvMixerCPU(nn.Module):
         return x / (1.0 + self.eps) ** 0.5
 
     @torch.no_grad()
-    def forward(self, x):
+    def trunk(self, x, blocks=None):
+        """Feature maps after the patch embedding and the first `blocks` blocks (all by default)."""
         x = x.float()
         x = self._bn(self._act(F.conv2d(x, self.patch_w, stride=self.p)))
-        for i in range(self.depth):
+        for i in range(self.depth if blocks is None else blocks):
             y = F.conv2d(x, self.dw_w[i], padding=self.k // 2, groups=self.dim)
             x = self._bn(self._act(y)) + x
             x = self._bn(self._act(F.conv2d(x, self.pw_w[i])))
-        x = x.mean(dim=(2, 3))
+        return x
+
+    @torch.no_grad()
+    def forward(self, x):
+        x = self.trunk(x).mean(dim=(2, 3))
         return F.linear(x, self.head_w)
 
 

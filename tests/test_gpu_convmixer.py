@@ -43,13 +43,26 @@ def test_convmixer_fused_matches_fp32_cpu(name):
     rel_torch, rel_fused = _rel(y_torch, ref), _rel(y_fused, ref)
     print(f"ConvMixer-{name}: rel(max|diff|/mean|ref|) torch-fp16 {rel_torch:.4f}, engine-fused {rel_fused:.4f}")
     assert rel_fused <= max(1.5 * rel_torch, 0.01)
-    assert (y_fused.float().cpu().argmax(1) == ref.argmax(1)).all()
+    # The random-init network shrinks its signal block by block (1x1 conv gain ~0.8, GELU ~0.5 near 0),
+    # so the logits are ~1e-5 and their argmax is noise.  Compare early feature maps, where every
+    # value is well inside the fp16 range: patch embedding + 3 blocks.
+    cpu3 = convmixer_cpu(name, seed=0).trunk(x, blocks=3)
+    with torch.no_grad():
+        t3 = base.model[:6](xd).float().cpu()
+        f3 = fused.model[:6](xd).float().cpu()
+    rel_t3 = ((t3 - cpu3).norm() / cpu3.norm()).item()
+    rel_f3 = ((f3 - cpu3).norm() / cpu3.norm()).item()
+    print(f"ConvMixer-{name} after 3 blocks: rel-L2 torch-fp16 {rel_t3:.2e}, engine-fused {rel_f3:.2e}")
+    assert rel_f3 <= max(1.5 * rel_t3, 2e-3)
 
 
 def test_convmixer_cuda_graph_replay_tracks_inputs():
     from depthwise_conv_b200.convmixer import convmixer, fuse_dw_blocks
 
-    model = fuse_dw_blocks(convmixer("1536_20", seed=0).half().cuda().to(memory_format=torch.channels_last))
+    full = fuse_dw_blocks(convmixer("1536_20", seed=0).half().cuda().to(memory_format=torch.channels_last))
+    # patch embedding + 3 blocks: the random-init network's signal decays with depth, so later
+    # feature maps (and the logits) can round to the same fp16 values for different images
+    model = full.model[:6]
     mk = lambda: torch.randn(1, 3, 224, 224, device="cuda").half().contiguous(memory_format=torch.channels_last)  # noqa: E731
     static_in = mk()
     s = torch.cuda.Stream()
