@@ -301,7 +301,7 @@ def run_ours(args):
     peaks = measured_peaks()
     traffic = profiled_traffic().get("convmixer1536_dw_layer")
     dw_gbs = dw_bytes(Bd, H, W, C, K) / (dw_us * 1e-6) / 1e9
-    plan = _lib.plan_query(Bd, H, W, C, K)
+    plan = _lib.plan_select(Bd, H, W, C, K)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -418,7 +418,7 @@ def run_dw(args):
     by = dw_bytes(Bg, H, W, C, K, epilogue=False) + (3 * 2 * C if epi else 0)
     achieved = fl / (us_layer * 1e-6) / 1e12
     peaks = measured_peaks()
-    plan = _lib.plan_query(max(1, -(-Bg // world)), H, W, C, K, accum)
+    plan = _lib.plan_select(max(1, -(-Bg // world)), H, W, C, K, accum)
     line = {
         "metric": "DW-conv µs/layer", "value": us_layer, "unit": "us/layer", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": us_layer / 1000.0, "higher_is_better": False,

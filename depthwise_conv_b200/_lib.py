@@ -64,6 +64,7 @@ SIGNATURES = {
     "dwb_abi_version": ([], _i),
     "dwb_status_string": ([_i], ctypes.c_char_p),
     "dwb_plan_query": ([ctypes.POINTER(Problem), _i, _i, ctypes.POINTER(Plan)], _i),
+    "dwb_plan_select": ([ctypes.POINTER(Problem), ctypes.POINTER(Plan)], _i),
     "dwb_plan_candidates": ([ctypes.POINTER(Problem), _i, _i, ctypes.POINTER(Plan), _i, ctypes.POINTER(_i)], _i),
     "dwb_last_error": ([], ctypes.c_char_p),
     "dwb_conv2d_nhwc_fwd_planned": ([_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i, _i,
@@ -145,6 +146,14 @@ def plan_query(B: int, H: int, W: int, C: int, K: int, accum: int = ACCUM_DEFAUL
     pr = Problem(B, H, W, C, K, accum)
     out = Plan()
     check("dwb_plan_query", load().dwb_plan_query(ctypes.byref(pr), sm_count, smem_optin, ctypes.byref(out)))
+    return out.as_dict()
+
+
+def plan_select(B: int, H: int, W: int, C: int, K: int, accum: int = ACCUM_DEFAULT) -> dict:
+    """The plan the launcher uses on the current device (tuned table, else the cost model)."""
+    pr = Problem(B, H, W, C, K, accum)
+    out = Plan()
+    check("dwb_plan_select", load().dwb_plan_select(ctypes.byref(pr), ctypes.byref(out)))
     return out.as_dict()
 
 

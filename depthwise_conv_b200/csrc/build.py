@@ -37,7 +37,7 @@ def _nvcc() -> str:
 
 
 def _headers_mtime() -> float:
-    paths = [os.path.join(HERE, f) for f in os.listdir(HERE) if f.endswith((".cuh", ".h"))]
+    paths = [os.path.join(HERE, f) for f in os.listdir(HERE) if f.endswith((".cuh", ".h", ".inc"))]
     paths += [os.path.join(INCLUDE, f) for f in os.listdir(INCLUDE) if f.endswith(".h")]
     paths.append(os.path.abspath(__file__))
     return max(os.path.getmtime(p) for p in paths)

@@ -342,7 +342,51 @@ static int launch_plan(DeviceState* st, const dwb_plan& plan, const void* x, con
   return DWB_OK;
 }
 
-// The planner's choice for a problem on this device, computed once.
+// Plans measured fastest on B200 (depthwise_conv_b200/tune.py).  A problem
+// with the same H, W, C, K and accumulation takes the entry with the nearest
+// batch (the tile shape does not depend on the batch); the plan is checked
+// against this device before use.
+struct TunedPlan {
+  long long B, H, W, C;
+  int K, accum, R, M, tile_h, tile_w, ring_rows, ring_wrows, grid;
+};
+static const TunedPlan kTunedPlans[] = {
+#include "dw_tuned_plans.inc"
+};
+
+static bool tuned_plan(DeviceState* st, const dwb_problem& pr, dwb_plan* out) {
+  const TunedPlan* best = nullptr;
+  long long best_d = 0;
+  for (const TunedPlan& t : kTunedPlans) {
+    if (t.H != pr.height || t.W != pr.width || t.C != pr.channels || t.K != pr.kernel_size || t.accum != pr.accum)
+      continue;
+    const long long d = t.B > pr.batch ? t.B - pr.batch : pr.batch - t.B;
+    if (!best || d < best_d) {
+      best = &t;
+      best_d = d;
+    }
+  }
+  if (!best) return false;
+  dwb_plan p;
+  std::memset(&p, 0, sizeof(p));
+  p.kernel_size = best->K;
+  p.accum = best->accum;
+  p.cols_per_thread = best->R;
+  p.rows_per_thread = best->M;
+  p.tile_h = best->tile_h;
+  p.tile_w = best->tile_w;
+  p.ring_rows = best->ring_rows;
+  p.ring_wrows = best->ring_wrows;
+  p.grid = best->grid;
+  const int regs = regs_of_variant(p.kernel_size, p.cols_per_thread, p.rows_per_thread, p.accum, st);
+  if (regs <= 0 || check_plan(pr, st->hw, regs, &p) != DWB_OK) return false;
+  p.ctas_per_sm = 0;  // not modelled for tuned plans
+  *out = p;
+  return true;
+}
+
+// The plan for a problem on this device (tuned table, else the planner's
+// cost model), computed once.
 static int cached_plan(DeviceState* st, const dwb_problem& pr, dwb_plan* out) {
   const PlanKey key{pr.batch, pr.height, pr.width, pr.channels, pr.kernel_size, pr.accum};
   {
@@ -353,8 +397,11 @@ static int cached_plan(DeviceState* st, const dwb_problem& pr, dwb_plan* out) {
       return DWB_OK;
     }
   }
-  const int rc = plan_problem(pr, st->hw, regs_of_variant, st, out);
-  if (rc != DWB_OK) return rc;
+  if (!tuned_plan(st, pr, out)) {
+    const int rc = plan_problem(pr, st->hw, regs_of_variant, st, out);
+    if (rc != DWB_OK) return rc;
+    out->grid = -1;  // persistent
+  }
   std::lock_guard<std::mutex> lk(st->plan_mu);
   if (st->plans.size() > 4096) st->plans.clear();  // bound the cache
   st->plans[key] = *out;
@@ -438,6 +485,16 @@ int dwb_plan_candidates(const dwb_problem* problem, int sm_count, int smem_optin
 }
 
 const char* dwb_last_error(void) { return g_last_error; }
+
+int dwb_plan_select(const dwb_problem* problem, dwb_plan* plan_out) {
+  if (!problem || !plan_out) return DWB_ERR_NULL_POINTER;
+  int rc = validate_problem(*problem);
+  if (rc != DWB_OK) return rc;
+  DeviceState* st = nullptr;
+  rc = get_device_state(&st);
+  if (rc != DWB_OK) return rc;
+  return cached_plan(st, *problem, plan_out);
+}
 
 int dwb_conv2d_nhwc_fwd_planned(const void* x, const void* w, const void* bias, const void* scale, const void* shift,
                                 const void* residual, void* y, int64_t B, int64_t H, int64_t W, int64_t C, int K,

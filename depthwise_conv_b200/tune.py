@@ -1,0 +1,127 @@
+"""Autotuner: time the planner's candidate plans on this GPU and write the tuned-plan table.
+
+    python -m depthwise_conv_b200.tune [--budget SECONDS] [--accum mixed|f32] [B,H,W,C,K ...]
+
+For every problem (default: the benchmark configurations) the candidates
+from ``dwb_plan_candidates`` are timed in the planner's cost order (CUDA
+graph of back-to-back launches, best of 3) until the per-problem time budget
+runs out; the fastest plan is written to ``csrc/dw_tuned_plans.inc``, which
+the library consults before its cost model (rebuild afterwards).  Results
+are also printed as JSON lines.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+TABLE = os.path.join(HERE, "csrc", "dw_tuned_plans.inc")
+
+DEFAULT_PROBLEMS = [
+    (1, 32, 32, 768, 7), (1, 32, 32, 1536, 9), (1, 16, 16, 1536, 9), (1, 32, 32, 1536, 13),
+    (1, 56, 56, 128, 31), (1, 28, 28, 256, 29), (1, 14, 14, 512, 27), (1, 7, 7, 1024, 13),
+    (16, 32, 32, 1536, 9), (64, 32, 32, 1536, 9), (128, 32, 32, 1536, 9), (256, 32, 32, 1536, 9),
+    (8, 56, 56, 1024, 7), (8, 56, 56, 1024, 31), (32, 56, 56, 1024, 9),
+] + [(64, 56, 56, 1024, k) for k in (7, 9, 13, 17, 21, 27, 29, 31)]
+
+FIELDS = ("cols_per_thread", "rows_per_thread", "tile_h", "tile_w", "ring_rows", "ring_wrows", "grid")
+
+
+def time_plan(d, x, w, y, plan, accum, reps):
+    import torch
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        d.conv2d_nhwc_fused(x, w, out=y, plan=plan, accum=accum)
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(reps):
+                d.conv2d_nhwc_fused(x, w, out=y, plan=plan, accum=accum)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    best = 1e30
+    for _ in range(3):
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1) / reps * 1000.0)
+    return best
+
+
+def tune_problem(B, H, W, C, K, accum, budget):
+    import torch
+    import depthwise_conv_b200 as d
+    from depthwise_conv_b200 import _lib
+
+    x = torch.randn(B, C, H, W, device="cuda").half().contiguous(memory_format=torch.channels_last)
+    w = (torch.randn(K, K, C, device="cuda") / K).half()
+    y = torch.empty_like(x)
+    cands = sorted(_lib.plan_candidates(B, H, W, C, K, accum), key=lambda c: c["model_cost"])
+    reps = 3 if B * H * W * C >= (64 << 20) else (10 if B >= 16 else 50)
+    default = time_plan(d, x, w, y, None, accum, reps)
+    best = (default, None)
+    t0 = time.time()
+    for c in cands:
+        for grid in (-1, 0):  # persistent, or one tile per CTA
+            plan = dict(c, grid=grid)
+            try:
+                us = time_plan(d, x, w, y, plan, accum, reps)
+            except RuntimeError:
+                continue
+            if us < best[0]:
+                best = (us, plan)
+        if time.time() - t0 > budget:
+            break
+    return default, best
+
+
+def write_table(rows, path):
+    lines = ["// dw_tuned_plans.inc -- plans measured fastest on B200 by depthwise_conv_b200/tune.py.",
+             "// {B, H, W, C, K, accum, R, M, tile_h, tile_w, ring_rows, ring_wrows, grid(-1 persistent, 0 one tile/CTA)}"]
+    old = []
+    if os.path.exists(TABLE):  # start from the committed table
+        for ln in open(TABLE):
+            ln = ln.strip()
+            if ln.startswith("{"):
+                old.append(ln)
+    keep = {}
+    for ln in old:
+        key = tuple(int(v) for v in ln.strip("{},").split(",")[:6])
+        keep[key] = ln
+    for (B, H, W, C, K, accum), plan in rows:
+        vals = [B, H, W, C, K, accum] + [int(plan[f]) for f in FIELDS]
+        keep[(B, H, W, C, K, accum)] = "{" + ", ".join(str(v) for v in vals) + "},"
+    lines += [keep[k] for k in sorted(keep)]
+    with open(path, "w") as f:
+        f.write("\n".join(lines) + "\n")
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("problems", nargs="*", help="B,H,W,C,K (default: the benchmark configurations)")
+    ap.add_argument("--budget", type=float, default=20.0, help="seconds of candidate timing per problem")
+    ap.add_argument("--accum", choices=["mixed", "f32"], default="mixed")
+    ap.add_argument("--no-write", action="store_true")
+    ap.add_argument("--out", default=TABLE, help="where to write the merged table (default: the library's)")
+    args = ap.parse_args()
+    from depthwise_conv_b200 import _lib
+    accum = _lib.ACCUM_MIXED if args.accum == "mixed" else _lib.ACCUM_F32
+    probs = [tuple(int(v) for v in p.split(",")) for p in args.problems] or DEFAULT_PROBLEMS
+    rows = []
+    for B, H, W, C, K in probs:
+        default, (us, plan) = tune_problem(B, H, W, C, K, accum, args.budget)
+        print(json.dumps({"problem": [B, H, W, C, K], "accum": args.accum, "default_us": default, "best_us": us,
+                          "plan": {f: plan[f] for f in FIELDS} if plan else None}), flush=True)
+        if plan is not None:
+            rows.append(((B, H, W, C, K, accum), plan))
+    if not args.no_write:
+        write_table(rows, args.out)
+        print("wrote", args.out)
+
+
+if __name__ == "__main__":
+    main()

@@ -106,6 +106,12 @@ DWB_API const char* dwb_status_string(int status);
 DWB_API int dwb_plan_query(const dwb_problem* problem, int sm_count, int smem_optin_bytes,
                    dwb_plan* plan_out);
 
+/* The plan the launcher uses for a problem on the current device: the tuned
+ * table entry measured fastest on B200 for the same H, W, C, K and
+ * accumulation (nearest batch), else the cost model with this device's
+ * register counts.  Needs a device. */
+DWB_API int dwb_plan_select(const dwb_problem* problem, dwb_plan* plan_out);
+
 /* Every feasible plan for a problem (host arithmetic only), in the planner's
  * enumeration order, for autotuning.  Writes at most `capacity` plans and
  * the total number of feasible plans to *count_out. */
