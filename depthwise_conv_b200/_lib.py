@@ -79,6 +79,7 @@ SIGNATURES = {
     "dwb_depthwise_31x31_128_nhwc": ([_p, _p, _p, _p, _i, _i, _i, _i, _p], _i),
     "dwb_depthwise_29x29_256_nhwc": ([_p, _p, _p, _p, _i, _i, _i, _i, _p], _i),
     "dwb_depthwise_27x27_512_nhwc": ([_p, _p, _p, _p, _i, _i, _i, _i, _p], _i),
+    "dwb_bias_act_affine_nhwc": ([_p, _p, _p, _p, _p, _i64, _i64, _i, _p], _i),
     "dwb_device_error": ([ctypes.POINTER(ctypes.c_int), _i, _p], _i),
     "dwb_probe_fma_peak": ([ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double), _p], _i),
 }

@@ -11,7 +11,8 @@ running var 1.
 ``fuse_dw_blocks`` swaps each Residual(DW conv, act, BN) for one
 ``depthwise::conv2d_nhwc_fused`` call that computes
 ``act(conv(x) + b) * s + t + x`` in a single kernel, with s, t the
-inference-mode BN fold (benchmark_cudnn_fused_e2e.py:115-134, :125-131).
+inference-mode BN fold (benchmark_cudnn_fused_e2e.py:115-134, :125-131), and
+each 1x1 conv -> act -> BN for a GEMM plus one fused elementwise kernel.
 """
 from __future__ import annotations
 
@@ -110,8 +111,62 @@ class FusedDWBlock(nn.Module):
                                                      self.act_code)
 
 
-def fuse_dw_blocks(model: ConvMixer) -> ConvMixer:
-    """Replace every Residual(DW conv, act, BN) of a ConvMixer with a FusedDWBlock."""
+class FusedPointwiseBlock(nn.Module):
+    """1x1 conv -> act -> BN as a cuBLAS GEMM on the NHWC pixels plus one elementwise pass.
+
+    channels_last data is a [B*H*W, C] row-major matrix, so the 1x1 convolution is
+    z = X @ W^T with no layout change; ``bias_act_affine`` then applies the bias,
+    the activation and the inference BatchNorm (scale/shift) in one kernel.
+    """
+
+    def __init__(self, conv: nn.Conv2d, act: str, bn: nn.BatchNorm2d):
+        super().__init__()
+        C_out, C_in = conv.out_channels, conv.in_channels
+        with torch.no_grad():
+            w = conv.weight.detach().reshape(C_out, C_in).t().contiguous().half()  # [C_in, C_out]
+            b = conv.bias.detach().half() if conv.bias is not None else torch.zeros(C_out, dtype=torch.float16)
+            scale = bn.weight / torch.sqrt(bn.running_var + bn.eps)
+            shift = bn.bias - bn.running_mean * scale
+        self.register_buffer("weight_t", w)
+        self.register_buffer("bias", b.contiguous())
+        self.register_buffer("scale", scale.half().contiguous())
+        self.register_buffer("shift", shift.half().contiguous())
+        self.act = act
+
+    def forward(self, x):
+        B, C, H, W = x.shape
+        z = torch.mm(x.permute(0, 2, 3, 1).reshape(B * H * W, C), self.weight_t)  # [BHW, C_out], NHWC
+        z = z.view(B, H, W, -1).permute(0, 3, 1, 2)  # channels_last view
+        return dw_ops.bias_act_affine(z, self.bias, self.scale, self.shift, self.act, out=z)
+
+
+class FusedStem(nn.Module):
+    """Patch conv -> act -> BN: cuDNN convolution without bias, then one elementwise pass."""
+
+    def __init__(self, conv: nn.Conv2d, act: str, bn: nn.BatchNorm2d):
+        super().__init__()
+        C = conv.out_channels
+        with torch.no_grad():
+            b = conv.bias.detach().half() if conv.bias is not None else torch.zeros(C, dtype=torch.float16)
+            scale = bn.weight / torch.sqrt(bn.running_var + bn.eps)
+            shift = bn.bias - bn.running_mean * scale
+        self.register_buffer("weight", conv.weight.detach().half().contiguous(memory_format=torch.channels_last))
+        self.register_buffer("bias", b.contiguous())
+        self.register_buffer("scale", scale.half().contiguous())
+        self.register_buffer("shift", shift.half().contiguous())
+        self.stride = conv.stride
+        self.act = act
+
+    def forward(self, x):
+        z = torch.nn.functional.conv2d(x, self.weight, None, self.stride)
+        if not z.is_contiguous(memory_format=torch.channels_last):
+            z = z.contiguous(memory_format=torch.channels_last)
+        return dw_ops.bias_act_affine(z, self.bias, self.scale, self.shift, self.act, out=z)
+
+
+def fuse_dw_blocks(model: ConvMixer, pointwise: bool = True) -> ConvMixer:
+    """Replace every Residual(DW conv, act, BN) of a ConvMixer with a FusedDWBlock and, with
+    ``pointwise``, every 1x1 conv -> act -> BN with a FusedPointwiseBlock."""
     n = 0
     for block in model.model:
         if not isinstance(block, nn.Sequential):
@@ -123,5 +178,15 @@ def fuse_dw_blocks(model: ConvMixer) -> ConvMixer:
                     act_name = 'relu' if isinstance(act, nn.ReLU) else 'gelu'
                     block[i] = FusedDWBlock(conv, act_name, bn).to(conv.weight.device)
                     n += 1
+        if pointwise and len(block) == 4 and isinstance(block[1], nn.Conv2d) and block[1].kernel_size == (1, 1):
+            conv, act, bn = block[1], block[2], block[3]
+            act_name = 'relu' if isinstance(act, nn.ReLU) else 'gelu'
+            fused = FusedPointwiseBlock(conv, act_name, bn).to(conv.weight.device)
+            block[1], block[2], block[3] = fused, nn.Identity(), nn.Identity()
+    if pointwise and isinstance(model.model[0], nn.Conv2d) and isinstance(model.model[2], nn.BatchNorm2d):
+        conv, act, bn = model.model[0], model.model[1], model.model[2]
+        act_name = 'relu' if isinstance(act, nn.ReLU) else 'gelu'
+        model.model[0] = FusedStem(conv, act_name, bn).to(conv.weight.device)
+        model.model[1], model.model[2] = nn.Identity(), nn.Identity()
     model.fused_blocks = n
     return model

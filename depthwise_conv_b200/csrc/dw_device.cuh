@@ -153,9 +153,42 @@ __device__ __forceinline__ f32x2 f32x2_zero() { return 0ull; }
 
 enum : int { kActNone = 0, kActRelu = 1, kActGelu = 2 };
 
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// Exact-form GELU, v * Phi(v) = 0.5 v erfc(-v / sqrt 2), with erfc from the
+// rational approximation 7.1.26 of Abramowitz & Stegun (Handbook of
+// Mathematical Functions, 1964): for a >= 0,
+//   erfc(a) = (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-a^2),
+//   t = 1 / (1 + p a),  |error| <= 1.5e-7,
+// used directly on the negative side (where the product is small and its
+// relative accuracy matters) and as 1 - erfc on the positive side.  About a
+// dozen instructions, two on the special-function unit; the result is within
+// one fp16 ulp of the exact GELU over the whole fp16 range.
+__device__ __forceinline__ float gelu_erf(float v) {
+  const float a = fabsf(v) * 0.70710678118654752f;  // |v| / sqrt(2)
+  const float t = rcp_approx(fmaf(0.3275911f, a, 1.0f));
+  float poly = fmaf(1.061405429f, t, -1.453152027f);
+  poly = fmaf(poly, t, 1.421413741f);
+  poly = fmaf(poly, t, -0.284496736f);
+  poly = fmaf(poly, t, 0.254829592f);
+  poly *= t;
+  const float ec = poly * ex2_approx(-a * a * 1.4426950408889634f);  // erfc(a)
+  const float hv = 0.5f * v;
+  return v >= 0.0f ? fmaf(-hv, ec, v) : hv * ec;  // v (1 - erfc/2)  |  v erfc / 2
+}
+
 __device__ __forceinline__ float apply_act(float v, int act) {
   if (act == kActRelu) return fmaxf(v, 0.0f);
-  if (act == kActGelu) return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+  if (act == kActGelu) return gelu_erf(v);
   return v;
 }
 

@@ -120,6 +120,24 @@ def conv2d_nhwc_fused(x: torch.Tensor, w: torch.Tensor, bias=None, scale=None, s
     return y
 
 
+def bias_act_affine(x: torch.Tensor, bias=None, scale=None, shift=None, act: int | str = 0,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = act(x + bias) * scale + shift per channel, for a channels_last fp16 CUDA tensor [B, C, H, W]."""
+    check_input(x)
+    B, C, H, W = x.shape
+    act_code = ACT_CODES[act] if isinstance(act, str) else int(act)
+    bp = check_vec(bias, C, "bias", x.device)
+    sp = check_vec(scale, C, "scale", x.device)
+    hp = check_vec(shift, C, "shift", x.device)
+    y = torch.empty_like(x) if out is None else out
+    if out is not None:
+        check_input(out, "out")
+    with _DeviceGuard(x.device):
+        _lib.call("dwb_bias_act_affine_nhwc", x.data_ptr(), bp or None, sp or None, hp or None, y.data_ptr(),
+                  B * H * W, C, act_code, _stream_of(x))
+    return y
+
+
 def conv2d_nhwc(x: torch.Tensor, w: torch.Tensor, bias=None) -> torch.Tensor:
     """y = conv(x, w) (+ bias): the plain depthwise convolution."""
     return conv2d_nhwc_fused(x, w, bias=bias)

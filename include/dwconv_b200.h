@@ -147,6 +147,15 @@ DWB_API int dwb_conv2d_nhwc_fwd_planned(const void* x, const void* w, const void
                                         int64_t B, int64_t H, int64_t W, int64_t C, int K,
                                         int act, const dwb_plan* plan, void* stream);
 
+/* y = act(x + bias) * scale + shift over `pixels` NHWC pixels of C channels
+ * (x, y fp16, 16-byte aligned, C % 8 == 0; bias/scale/shift [C] or NULL).
+ * The elementwise tail of a ConvMixer pointwise block (1x1 conv -> bias ->
+ * act -> BatchNorm, convmixer/convmixer.py:116-118) in one pass; x == y is
+ * allowed.  No counterpart kernel in the reference (PyTorch ops there). */
+DWB_API int dwb_bias_act_affine_nhwc(const void* x, const void* bias, const void* scale,
+                                     const void* shift, void* y, int64_t pixels, int64_t C,
+                                     int act, void* stream);
+
 /* ---- reference-facing entry points --------------------------------------
  * One per launcher of luckychen/depthwise_conv on this path, with the same
  * argument meaning.  Where the reference loops over the batch in Python

@@ -196,6 +196,35 @@ def test_cuda_graph_capture_of_c_abi(eng, oracle_mod):
     check(oracle_mod, y, exact2, "graph replay 2")
 
 
+@pytest.mark.parametrize("act", ["none", "relu", "gelu"])
+def test_bias_act_affine(eng, act):
+    """The pointwise-block epilogue: y = act(x + b) * s + t, against float64 math."""
+    from math import erf, sqrt
+    rng = np.random.default_rng(3)
+    B, C, H, W = 2, 1536, 7, 9
+    x = (rng.standard_normal((B, H, W, C)) * 2).astype(np.float16)
+    b = (rng.standard_normal(C) * 0.5).astype(np.float16)
+    s = rng.uniform(0.5, 1.5, C).astype(np.float16)
+    t = (rng.standard_normal(C) * 0.5).astype(np.float16)
+    v = x.astype(np.float64) + b.astype(np.float64)
+    if act == "relu":
+        v = np.maximum(v, 0)
+    elif act == "gelu":
+        v = 0.5 * v * (1 + np.vectorize(erf)(v / sqrt(2)))
+    exact = v * s.astype(np.float64) + t.astype(np.float64)
+    xd = to_dev(x)
+    y = eng.dw_ops.bias_act_affine(xd, to_dev(b), to_dev(s), to_dev(t), act)
+    torch.cuda.synchronize()
+    got = to_host(y).astype(np.float64)
+    a = np.abs(exact)
+    ulp = 2.0 ** (np.floor(np.log2(np.maximum(a, 2.0 ** -14))) - 10)
+    assert (np.abs(got - exact) <= 2 * ulp + 1e-7).all()
+    # in place (x == y), as the ConvMixer pointwise block uses it
+    eng.dw_ops.bias_act_affine(xd, to_dev(b), to_dev(s), to_dev(t), act, out=xd)
+    torch.cuda.synchronize()
+    assert torch.equal(xd, y)
+
+
 def test_probe_fma_peak_reports_plausible_rates(eng):
     h, f = eng.probe_fma_peak()
     assert 10.0 < h < 200.0 and 10.0 < f < 200.0

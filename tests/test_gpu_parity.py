@@ -139,6 +139,21 @@ def test_fused_epilogue(eng, oracle_mod, act, terms):
     assert_parity(oracle_mod, y, exact, what=f"{terms}/{act}")
 
 
+def test_gelu_over_its_whole_range(eng, oracle_mod):
+    """K=1 with unit weights makes the convolution the identity, so y = act(x + bias):
+    the GELU is checked from deep negative to large positive arguments."""
+    C, H, W = 64, 16, 16
+    rng = np.random.default_rng(5)
+    x = (rng.standard_normal((1, H, W, C)) * 3.0).astype(np.float16)
+    w = np.ones((1, 1, C), np.float16)
+    bias = np.linspace(-8.0, 8.0, C).astype(np.float16)
+    exact, _ = oracle_mod.dw_forward(x, w, bias, None, None, None, "gelu")
+    for accum in (0, 1):
+        y = to_host(run_engine(eng, x, w, bias, None, None, False, "gelu", accum)).astype(np.float64)
+        err = np.abs(y - exact)
+        assert (err <= 2.0 * ulp16(exact) + 1e-7).all(), f"GELU off by {err.max():.3e} (accum={accum})"
+
+
 # ---------------------------------------------------------------- BASELINE configs
 
 B1_CONFIGS = [  # (name, B, H, W, C, K, weight std)
