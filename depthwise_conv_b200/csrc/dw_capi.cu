@@ -229,15 +229,6 @@ static int encode_w_map(CUtensorMap* m, const void* w, long long C, int K) {
 
 static inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-// Mixed accumulation: kernel rows per fp16 chain.  A chain of L fp16
-// roundings leaves a relative error of about 2e-4 * sqrt(L / 2) (random
-// walk of half-ulp roundings); chains cover one kernel row (K >= 25 rows are
-// split in two by the kernel itself), so L <= 16.
-static int mixed_chain_rows(int K) {
-  (void)K;
-  return 1;  // one kernel row per chain: the partials stay step-local (fewer registers)
-}
-
 // Argument checks shared by every entry point (no CUDA calls).  An empty
 // batch is accepted before the pointer checks: an empty tensor may report a
 // null data pointer.
@@ -301,14 +292,21 @@ static int launch_plan(DeviceState* st, const dwb_plan& plan, const void* x, con
   if (plan.tiles > 0x7fffffffLL) return DWB_ERR_BAD_SHAPE;
   p.num_tiles = static_cast<uint32_t>(plan.tiles);
   p.ncg = plan.tile_w / plan.cols_per_thread;
+  p.nsplit = plan.row_splits > 1 ? plan.row_splits : 1;
+  p.slots = p.ncg * (plan.tile_h / plan.rows_per_thread);
   p.consumer_warps = plan.consumer_warps;
+  if (p.consumer_warps != p.nsplit * p.slots) return DWB_ERR_BAD_ARG;
   p.ring_rows = plan.ring_rows;
   p.ring_wrows = plan.ring_wrows;
   p.act = act;
   p.x_ring_off = kBarrierBytes;
   p.w_ring_off = kBarrierBytes + static_cast<uint32_t>(plan.ring_rows) * plan.tile_w_in * kPixelBytes;
+  long long red_off = 0;
+  const long long smem_need = plan_smem_bytes(K, plan.tile_w_in, plan.ring_rows, plan.ring_wrows, p.nsplit, p.slots,
+                                              plan.rows_per_thread, plan.cols_per_thread, &red_off);
+  if (smem_need > plan.smem_bytes) return DWB_ERR_BAD_ARG;
+  p.red_off = static_cast<uint32_t>(red_off);
   p.err = st->err_word;
-  p.chain_rows = mixed_chain_rows(K);
 
   // grid < 0: persistent, as many CTAs as fit on the device at once (measured
   // by the occupancy calculator for this variant); otherwise the plan's CTA
@@ -349,6 +347,7 @@ static int launch_plan(DeviceState* st, const dwb_plan& plan, const void* x, con
 struct TunedPlan {
   long long B, H, W, C;
   int K, accum, R, M, tile_h, tile_w, ring_rows, ring_wrows, grid;
+  int splits;  // row split (0 or 1 = none)
 };
 static const TunedPlan kTunedPlans[] = {
 #include "dw_tuned_plans.inc"
@@ -378,6 +377,7 @@ static bool tuned_plan(DeviceState* st, const dwb_problem& pr, dwb_plan* out) {
   p.ring_rows = best->ring_rows;
   p.ring_wrows = best->ring_wrows;
   p.grid = best->grid;
+  p.row_splits = best->splits;
   const int regs = regs_of_variant(p.kernel_size, p.cols_per_thread, p.rows_per_thread, p.accum, st);
   if (regs <= 0 || check_plan(pr, st->hw, regs, &p) != DWB_OK) return false;
   p.ctas_per_sm = 0;  // not modelled for tuned plans

@@ -12,7 +12,7 @@ namespace dwb {
 
 // Error codes a kernel stores in the device error word (first writer wins)
 // when one of its bounded waits expires: 1 = input-row wait, 2 = weight-row
-// wait, 3 = ring-slot (empty) wait.  The word lives in the launcher's
+// wait, 3 = ring-slot (empty) wait, 4 = row-split partial-sum hand-off.  The word lives in the launcher's
 // translation unit; kernels receive its address.
 
 // ~1 s at 2 GHz: far above any legitimate wait (a row load takes ~1 us).
@@ -120,6 +120,11 @@ typedef unsigned long long f32x2;
 // acc += a * b, element-wise on the two lanes, each a single-rounding fp32 FMA.
 __device__ __forceinline__ void ffma2(f32x2& acc, f32x2 a, f32x2 b) {
   asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
+}
+
+// acc += b, element-wise on the two lanes.
+__device__ __forceinline__ void fadd2(f32x2& acc, f32x2 b) {
+  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(acc) : "l"(b));
 }
 
 // half2 (two channels) -> packed fp32 pair.

@@ -31,9 +31,19 @@
 //   input half2 is loaded once and feeds up to R outputs.
 //     ACC = 0: inputs and weights converted to fp32, packed fp32x2 FMAs
 //              (FFMA2) into fp32 accumulators -- every tap in fp32;
-//     ACC = 1: fp16x2 HFMA2 into short fp16 chains (chain_rows kernel rows,
-//              or half a row for K >= 25) that are added to the fp32
-//              accumulators when they end -- no conversion in the loop.
+//     ACC = 1: fp16x2 HFMA2 into short fp16 chains (one kernel row, or half
+//              a row for K >= 25) that are added to the fp32 accumulators
+//              when they end -- no conversion in the loop.
+//
+// Row split (S > 1, for small images where tiles are few)
+//   S warps share each output slot; warp group g computes the kernel rows
+//   s_lo + g, s_lo + g + S, ... into fp32 accumulators (group 0 starts from
+//   the bias, the others from zero).  At the end of the tile groups 1..S-1
+//   store their accumulators in a shared-memory exchange area and group 0
+//   adds them before the epilogue.  The hand-off is two mbarriers (partials
+//   written / area free again) with bounded waits, so a failing warp can
+//   never leave the others blocked.  Every warp still waits for and releases
+//   every ring slot in order, which keeps the ring protocol unchanged.
 //
 // Epilogue (fused): v = acc + bias; v = act(v); v = v * scale + shift;
 //   v += residual; stored as half2, 128 contiguous bytes per warp.
@@ -59,12 +69,14 @@ struct DwParams {
   int tiles_h, tiles_w, cblocks;
   uint32_t num_tiles;      // < 2^31 (checked by the launcher)
   int ncg;                 // column groups (warps across the tile width)
-  int consumer_warps;
+  int consumer_warps;                // nsplit * slots
+  int slots;                         // warps per split group (ncg * row groups)
+  int nsplit;                        // row split S (1 = none)
   int ring_rows, ring_wrows;
   int act;
   uint32_t x_ring_off, w_ring_off;  // byte offsets inside dynamic smem
+  uint32_t red_off;                 // partial-sum exchange area (S > 1)
   int* err;                         // device error word (bounded-wait expiry)
-  int chain_rows;                   // mixed mode: kernel rows per fp16 chain
 };
 
 // Geometry of one tile.
@@ -198,6 +210,8 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
   uint64_t* empty_x = full_x + RR;
   uint64_t* full_w = empty_x + RR;
   uint64_t* empty_w = full_w + RW;
+  uint64_t* red_full = empty_w + RW;   // row split: partial sums of a tile written
+  uint64_t* red_empty = red_full + 1;  // row split: exchange area free again
   unsigned char* xring = smem + p.x_ring_off;
   unsigned char* wring = smem + p.w_ring_off;
   const uint32_t row_bytes = static_cast<uint32_t>(p.tile_w_in) * kPixelBytes;
@@ -214,6 +228,10 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
     for (int i = 0; i < RW; ++i) {
       mbar_init(&full_w[i], 1);
       mbar_init(&empty_w[i], p.consumer_warps);
+    }
+    if (p.nsplit > 1) {
+      mbar_init(red_full, (p.nsplit - 1) * p.slots * 32);  // one arrival per thread of groups 1..S-1
+      mbar_init(red_empty, p.slots * 32);                  // one arrival per thread of group 0
     }
     fence_mbar_init();
   }
@@ -262,8 +280,10 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
   }
 
   // ---------------- consumer warps ----------------
-  const int rg = warp / p.ncg;
-  const int cg = warp - rg * p.ncg;
+  const int sg = warp / p.slots;            // split group: kernel rows st = sg (mod nsplit)
+  const int slot_id = warp - sg * p.slots;  // output slot within the tile
+  const int rg = slot_id / p.ncg;
+  const int cg = slot_id - rg * p.ncg;
   const int trow0 = rg * M;  // first tile row of this warp
   const int col0 = cg * R;   // first tile column of this warp
   const int xoff = col0 * kPixelH2 + lane;  // half2 offset of this thread's first input column
@@ -275,8 +295,9 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
 
   f32x2 bias = 0, scale = 0, shift = 0;
   int bias_c0 = -1;
+  uint32_t tile_iter = 0;  // tiles this CTA has finished (phase of the split hand-off)
 
-  for (uint32_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+  for (uint32_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++tile_iter) {
     const TileInfo ti = decode_tile<K>(p, t);
 
     // per-channel epilogue parameters, reloaded when the tile's channels change
@@ -295,10 +316,11 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
     }
 
     f32x2 acc[M][R];  // packed fp32 (channel 2l, channel 2l+1), starting from the bias
+    const f32x2 acc0 = sg == 0 ? bias : f32x2_zero();
 #pragma unroll
     for (int m = 0; m < M; ++m)
 #pragma unroll
-      for (int r = 0; r < R; ++r) acc[m][r] = bias;
+      for (int r = 0; r < R; ++r) acc[m][r] = acc0;
     __half2 part[M][SPLIT][R];  // mixed mode fp16 chains (unused in fp32 mode)
 #pragma unroll
     for (int m = 0; m < M; ++m)
@@ -306,7 +328,7 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
       for (int c = 0; c < SPLIT; ++c)
 #pragma unroll
         for (int r = 0; r < R; ++r) part[m][c][r] = __float2half2_rn(0.f);
-    int chain_steps = 0;
+    int turn = sg;  // steps until this warp's next kernel row
 
     // warps whose columns all lie right of the image have nothing to compute
     const bool any_col = ti.w0 + col0 < p.W;
@@ -336,15 +358,14 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
       const __half2* xrow1 = reinterpret_cast<const __half2*>(xring + slot1 * row_bytes) + xoff;
       const int out0 = ti.h0 + trow0;
       const int in0 = out0 - PAD + s;
-      const bool v0 = any_col && out0 < p.H && in0 >= 0 && in0 < p.H;                        // warp-uniform
-      const bool v1 = any_col && M == 2 && out0 + 1 < p.H && in0 + 1 >= 0 && in0 + 1 < p.H;  // warp-uniform
+      const bool mine = turn == 0;  // warp-uniform
+      turn = mine ? p.nsplit - 1 : turn - 1;
+      const bool v0 = mine && any_col && out0 < p.H && in0 >= 0 && in0 < p.H;                        // warp-uniform
+      const bool v1 = mine && any_col && M == 2 && out0 + 1 < p.H && in0 + 1 >= 0 && in0 + 1 < p.H;  // warp-uniform
 
       if (v0 || v1) {
         step_rows<K, R, M, ACC>(acc, part, wrow, xrow0, xrow1, v0, v1);
-      }
-      if constexpr (ACC == 1) {
-        if (++chain_steps == p.chain_rows || st + 1 == ti.nsteps) {  // the fp16 chains end here
-          chain_steps = 0;
+        if constexpr (ACC == 1) {  // the fp16 chains of this kernel row end here
 #pragma unroll
           for (int m = 0; m < M; ++m)
 #pragma unroll
@@ -372,6 +393,37 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
     for (int q = ti.nsteps; q < ti.nrows; ++q) {
       if (lane == 0) mbar_arrive(&empty_x[rel_x.slot]);
       rel_x.next(RR);
+    }
+
+    // ---------------- row split: partial sums to group 0 ----------------
+    if (p.nsplit > 1) {
+      // exchange area: [group 1..S-1][slot][m][r][lane] packed fp32 pairs, so
+      // a warp's access to one (m, r) is 256 contiguous bytes
+      f32x2* red = reinterpret_cast<f32x2*>(smem + p.red_off) + lane;
+      constexpr int kSlotPairs = M * R * 32;
+      if (sg > 0) {
+        if (tile_iter > 0) {  // group 0 has read the previous tile's partials
+          ok = mbar_wait_bounded(red_empty, (tile_iter - 1) & 1u, p.err, 4);
+          if (!ok) break;
+        }
+        f32x2* dst = red + ((sg - 1) * p.slots + slot_id) * kSlotPairs;
+#pragma unroll
+        for (int m = 0; m < M; ++m)
+#pragma unroll
+          for (int r = 0; r < R; ++r) dst[(m * R + r) * 32] = acc[m][r];
+        mbar_arrive(red_full);  // every lane, after its own stores (release)
+        continue;
+      }
+      ok = mbar_wait_bounded(red_full, tile_iter & 1u, p.err, 4);
+      if (!ok) break;
+      for (int g = 1; g < p.nsplit; ++g) {
+        const f32x2* src = red + ((g - 1) * p.slots + slot_id) * kSlotPairs;
+#pragma unroll
+        for (int m = 0; m < M; ++m)
+#pragma unroll
+          for (int r = 0; r < R; ++r) fadd2(acc[m][r], src[(m * R + r) * 32]);
+      }
+      mbar_arrive(red_empty);  // every lane, after its own loads
     }
 
     // ---------------- fused epilogue ----------------

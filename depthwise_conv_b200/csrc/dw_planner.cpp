@@ -36,6 +36,8 @@ constexpr int kBarrierBytes = 1024;
 constexpr int kMaxConsumerWarps = 16;
 constexpr int kMaxBoxDim = 256;  // TMA box limit per dimension
 constexpr double kLoadLatency = 2000.0;  // clocks from TMA issue to data (L2/HBM), modelled
+constexpr int kNumSplits = 5;
+constexpr int kSplits[kNumSplits] = {1, 2, 3, 4, 8};  // row splits the planner considers
 
 inline long long ceil_div(long long a, long long b) { return (a + b - 1) / b; }
 
@@ -64,6 +66,17 @@ int estimate_regs(int K, int R, int M, int acc) {
   int est = 2 * M * R + w + part + 28;
   return std::min(255, std::max(48, est));
 }
+
+long long plan_smem_bytes(int K, int tile_w_in, int ring_rows, int ring_wrows, int nsplit, int slots, int M, int R,
+                          long long* red_off) {
+  long long off = kBarrierBytes + static_cast<long long>(ring_rows) * tile_w_in * kPixelBytes +
+                  static_cast<long long>(ring_wrows) * K * kPixelBytes;
+  if (red_off) *red_off = off;
+  if (nsplit > 1) off += static_cast<long long>(nsplit - 1) * slots * M * R * 32 * 8;
+  return off;
+}
+
+bool barriers_fit(int ring_rows, int ring_wrows) { return (2 * (ring_rows + ring_wrows) + 2) * 8 <= kBarrierBytes; }
 
 int validate_problem(const dwb_problem& pr) {
   const long long B = pr.batch, H = pr.height, W = pr.width, C = pr.channels;
@@ -102,10 +115,17 @@ int enumerate_plans(const dwb_problem& pr, const HwInfo& hw, RegsFn regs, void* 
         for (int nrg = 1; nrg * ncg <= kMaxConsumerWarps; ++nrg) {
           const int tile_h = nrg * M;
           if (tile_h > H + M - 1) break;  // taller tiles only add empty rows
-          const int consumer_warps = nrg * ncg;
+          const int slots = nrg * ncg;
+         for (int si = 0; si < kNumSplits; ++si) {
+          const int nsplit = kSplits[si];
+          if (nsplit * slots > kMaxConsumerWarps || nsplit > K) break;
+          const int consumer_warps = nsplit * slots;
           const int threads = (consumer_warps + 1) * 32;
           const int cps_regs = ctas_by_registers(rg, consumer_warps + 1, hw.regs_per_sm);
           if (cps_regs < 1) break;
+          // splitting only pays where tiles are too few to fill the device
+          const long long tiles_all = B * ceil_div(H, tile_h) * ceil_div(W, tile_w) * cblocks;
+          if (nsplit > 1 && tiles_all * slots > 16LL * hw.sm_count) break;
           const long long tiles_h = ceil_div(H, tile_h);
           const long long tiles = B * tiles_h * tiles_w * cblocks;
           if (tiles > (1LL << 40)) continue;
@@ -123,29 +143,34 @@ int enumerate_plans(const dwb_problem& pr, const HwInfo& hw, RegsFn regs, void* 
             const int nsteps = std::max(0, s_hi - s_lo);
             double valid = 0.0;
             for (int i = 0; i < rows_in; ++i) valid += valid_taps(h0 + i, static_cast<int>(H), K);
-            // per warp column group: every row group walks all steps
+            // per warp column group: every row group walks all steps (the
+            // weight conversion is paid by every split group)
             work_sum += ncg * (valid * row_cost + static_cast<double>(nsteps) * nrg * wrow_cost);
             bytes_sum += (static_cast<double>(nsteps + tile_h - 1) * tile_w_in + nsteps * K) * kPixelBytes;
             steps_sum += nsteps;
           }
-          const double work_cta = work_sum / static_cast<double>(tiles_h);
+          // row split: groups 1..S-1 hand M*R fp32 pairs per slot to group 0
+          const double red_cost = nsplit > 1 ? static_cast<double>(nsplit) * slots * M * R * 4.0 + 600.0 : 0.0;
+          const double work_cta = work_sum / static_cast<double>(tiles_h) + red_cost;
           const double bytes_cta = bytes_sum / static_cast<double>(tiles_h);
           const double steps_cta = steps_sum / static_cast<double>(tiles_h);
           const long long tiles_busiest = ceil_div(tiles, hw.sm_count);  // tiles on the busiest SM
 
           // Prefetch depth (rows the producer may run ahead of the consumers):
           // deeper rings hide the load latency, shallower ones fit more CTAs.
+          // A row split keeps S steps in flight, so its rings are S - 1 rows deeper.
           int last_ring = -1;
           const int depths[4] = {2, 4, 8, K + 64};
           for (int di = 0; di < 4; ++di) {
-            const int ring_rows = std::min(tile_h + depths[di], tile_h + K - 1);
+            const int ring_rows = std::min(tile_h + nsplit - 1 + depths[di], tile_h + K - 1);
             if (ring_rows == last_ring) continue;
             last_ring = ring_rows;
-            const int ring_wrows = std::min(std::max(3, depths[di] + 1), K);
-            const long long smem = kBarrierBytes + static_cast<long long>(ring_rows) * tile_w_in * kPixelBytes +
-                                   static_cast<long long>(ring_wrows) * K * kPixelBytes;
+            const int ring_wrows = std::min(std::max(3, nsplit + depths[di]), K);
+            long long red_off = 0;
+            const long long smem =
+                plan_smem_bytes(K, tile_w_in, ring_rows, ring_wrows, nsplit, slots, M, R, &red_off);
             if (smem > hw.smem_optin) break;
-            if (2 * (ring_rows + ring_wrows) * 8 > kBarrierBytes) break;
+            if (!barriers_fit(ring_rows, ring_wrows)) break;
             const int cps = static_cast<int>(std::min<long long>(
                 {hw.smem_per_sm / (smem + hw.smem_reserved), static_cast<long long>(cps_regs),
                  hw.max_threads_sm / threads, hw.max_ctas_sm}));
@@ -164,7 +189,9 @@ int enumerate_plans(const dwb_problem& pr, const HwInfo& hw, RegsFn regs, void* 
             const double tiles_per_cta = std::ceil(static_cast<double>(tiles) / static_cast<double>(grid));
             const double ahead = static_cast<double>(ring_rows - tile_h + 1);  // steps of lookahead
             const double t_lat = kLoadLatency + tiles_per_cta * (steps_cta * kLoadLatency / ahead + 300.0);
-            const double cost = std::max(t_tp, t_lat) + tiles_per_cta * 300.0;
+            // critical path of one warp: its share of the slot's kernel rows, serially
+            const double t_warp = tiles_per_cta * work_cta / consumer_warps;
+            const double cost = std::max({t_tp, t_lat, t_warp}) + tiles_per_cta * 300.0;
           dwb_plan pl;
           std::memset(&pl, 0, sizeof(pl));
           pl.kernel_size = K;
@@ -185,9 +212,11 @@ int enumerate_plans(const dwb_problem& pr, const HwInfo& hw, RegsFn regs, void* 
           pl.accum = pr.accum;
           pl.regs_estimate = rg;
           pl.model_cost = cost;
+          pl.row_splits = nsplit;
           ++count;
           if (sink) sink(pl, sink_ctx);
           }
+         }
         }
       }
     }
@@ -230,15 +259,20 @@ int check_plan(const dwb_problem& pr, const HwInfo& hw, int regs, dwb_plan* p) {
   if (!variant_compiled(K, R, M, p->accum) || p->kernel_size != K || p->accum != pr.accum) return DWB_ERR_BAD_ARG;
   if (p->tile_w < R || p->tile_w % R != 0 || p->tile_h < M || p->tile_h % M != 0) return DWB_ERR_BAD_ARG;
   if (p->tile_w + K - 1 > kMaxBoxDim) return DWB_ERR_BAD_ARG;
-  const int cw = (p->tile_w / R) * (p->tile_h / M);
-  if (cw < 1 || cw > 31) return DWB_ERR_BAD_ARG;
-  if (p->ring_rows < p->tile_h || p->ring_rows > 60 || p->ring_wrows < 1 || p->ring_wrows > K) return DWB_ERR_BAD_ARG;
+  if (p->row_splits == 0) p->row_splits = 1;  // plans from callers that predate the field
+  const int S = p->row_splits;
+  if (S < 1 || S > K) return DWB_ERR_BAD_ARG;
+  const int slots = (p->tile_w / R) * (p->tile_h / M);
+  const int cw = S * slots;
+  if (slots < 1 || cw > 31) return DWB_ERR_BAD_ARG;
+  if (p->ring_rows < p->tile_h || p->ring_wrows < 1 || p->ring_wrows > K) return DWB_ERR_BAD_ARG;
+  if (!barriers_fit(p->ring_rows, p->ring_wrows)) return DWB_ERR_BAD_ARG;
   p->channel_block = kChannelsPerCta;
   p->tile_w_in = p->tile_w + K - 1;
   p->consumer_warps = cw;
   p->threads = 32 * (cw + 1);
-  const long long smem = kBarrierBytes + static_cast<long long>(p->ring_rows) * p->tile_w_in * kPixelBytes +
-                         static_cast<long long>(p->ring_wrows) * K * kPixelBytes;
+  p->reserved0 = 0;
+  const long long smem = plan_smem_bytes(K, p->tile_w_in, p->ring_rows, p->ring_wrows, S, slots, M, R, nullptr);
   if (smem > hw.smem_optin) return DWB_ERR_BAD_ARG;
   if (regs > 0 && ctas_by_registers(regs, cw + 1, hw.regs_per_sm) < 1) return DWB_ERR_BAD_ARG;
   p->smem_bytes = static_cast<int32_t>(smem);

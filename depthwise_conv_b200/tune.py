@@ -26,7 +26,7 @@ DEFAULT_PROBLEMS = [
     (8, 56, 56, 1024, 7), (8, 56, 56, 1024, 31), (32, 56, 56, 1024, 9),
 ] + [(64, 56, 56, 1024, k) for k in (7, 9, 13, 17, 21, 27, 29, 31)]
 
-FIELDS = ("cols_per_thread", "rows_per_thread", "tile_h", "tile_w", "ring_rows", "ring_wrows", "grid")
+FIELDS = ("cols_per_thread", "rows_per_thread", "tile_h", "tile_w", "ring_rows", "ring_wrows", "grid", "row_splits")
 
 
 def time_plan(d, x, w, y, plan, accum, reps):
@@ -81,7 +81,8 @@ def tune_problem(B, H, W, C, K, accum, budget):
 
 def write_table(rows, path):
     lines = ["// dw_tuned_plans.inc -- plans measured fastest on B200 by depthwise_conv_b200/tune.py.",
-             "// {B, H, W, C, K, accum, R, M, tile_h, tile_w, ring_rows, ring_wrows, grid(-1 persistent, 0 one tile/CTA)}"]
+             "// {B, H, W, C, K, accum, R, M, tile_h, tile_w, ring_rows, ring_wrows, grid(-1 persistent, 0 one tile/CTA),",
+             "//  row_splits}"]
     old = []
     if os.path.exists(TABLE):  # start from the committed table
         for ln in open(TABLE):

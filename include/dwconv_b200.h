@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define DWB_ABI_VERSION 1
+#define DWB_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define DWB_API __attribute__((visibility("default")))
@@ -93,6 +93,10 @@ typedef struct dwb_plan {
     int32_t accum;              /* dwb_accum actually used                      */
     int32_t regs_estimate;      /* registers/thread assumed by the planner      */
     double model_cost;          /* planner's modelled time (arbitrary units)     */
+    int32_t row_splits;         /* S: warps sharing one output slot, each taking
+                                   every S-th kernel row; their fp32 partial sums
+                                   are added in shared memory (0 or 1 = none)    */
+    int32_t reserved0;          /* zero                                          */
 } dwb_plan;
 
 /* ---- library information ------------------------------------------------ */

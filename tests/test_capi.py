@@ -39,7 +39,7 @@ def test_every_declared_symbol_is_exported_and_bound(lib):
 
 def test_abi_version_and_status_strings(lib):
     from depthwise_conv_b200 import _lib
-    assert lib.dwb_abi_version() == 1
+    assert lib.dwb_abi_version() == 2
     for code in range(9):
         assert lib.dwb_status_string(code) and b"unknown" not in lib.dwb_status_string(code)
     assert lib.dwb_status_string(99) == b"unknown status"
@@ -101,16 +101,35 @@ def test_plans_respect_hardware_limits(B, H, W, C, K, accum):
     assert (R in (7, 8, 14, 16) or (R in (28, 32) and K <= 13)) and M in (1, 2)
     assert p["tile_w"] % R == 0 and p["tile_h"] % M == 0
     assert p["tile_w_in"] == p["tile_w"] + K - 1 <= 256                 # TMA box limit
-    assert p["consumer_warps"] == (p["tile_w"] // R) * (p["tile_h"] // M)
+    S = p["row_splits"]
+    assert 1 <= S <= K
+    assert p["consumer_warps"] == S * (p["tile_w"] // R) * (p["tile_h"] // M)
     assert p["threads"] == 32 * (p["consumer_warps"] + 1) <= 1024
     # registers: per warp in units of 256, a CTA's warps spread over 4 sub-partitions of 16K each
     per_warp = -(-p["regs_estimate"] * 32 // 256) * 256
     assert -(-(p["consumer_warps"] + 1) // 4) * per_warp <= 16384
     assert p["smem_bytes"] <= 232448 and p["ctas_per_sm"] >= 1
     assert p["ring_rows"] >= p["tile_h"] and p["ring_wrows"] >= 1
+    assert (2 * (p["ring_rows"] + p["ring_wrows"]) + 2) * 8 <= 1024  # mbarrier area
+    ring = 1024 + p["ring_rows"] * p["tile_w_in"] * 128 + p["ring_wrows"] * K * 128
+    slots = p["consumer_warps"] // S
+    assert p["smem_bytes"] == ring + (S - 1) * slots * M * R * 32 * 8  # + partial-sum exchange area
     tiles = -(-H // p["tile_h"]) * -(-W // p["tile_w"]) * -(-C // 64)
     assert p["tiles"] == B * tiles
     assert 1 <= p["grid"] <= min(p["tiles"], p["ctas_per_sm"] * 148) or (B == 0 and p["grid"] == 0)
+
+
+def test_row_split_candidates_for_small_images():
+    """Small images with large kernels get plans whose warps split the kernel rows; big batches do not."""
+    from depthwise_conv_b200 import _lib
+    small = _lib.plan_candidates(1, 14, 14, 512, 27, 1)
+    splits = {c["row_splits"] for c in small}
+    assert {1, 2, 4} <= splits
+    for c in small:
+        assert c["consumer_warps"] <= 16 and c["consumer_warps"] % c["row_splits"] == 0
+        assert c["ring_rows"] >= c["tile_h"] + c["row_splits"] - 1 or c["ring_rows"] == c["tile_h"] + 26
+    big = _lib.plan_candidates(64, 56, 56, 1024, 9, 1)
+    assert {c["row_splits"] for c in big} == {1}
 
 
 def test_plan_rejects_bad_problems():
