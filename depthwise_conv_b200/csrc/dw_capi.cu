@@ -16,6 +16,7 @@
 
 #include "../../include/dwconv_b200.h"
 #include "dw_kernel.cuh"
+#include "dw_launch.h"
 #include "dw_planner.h"
 
 namespace dwb {
@@ -331,11 +332,11 @@ static int launch_plan(DeviceState* st, const dwb_plan& plan, const void* x, con
   }
 
   void* args[3] = {&tmx, &tmw, &p};
-  const cudaError_t ce = cudaLaunchKernel(e->fn, dim3(static_cast<unsigned>(grid)), dim3(plan.threads), args,
-                                          static_cast<size_t>(plan.smem_bytes), static_cast<cudaStream_t>(stream));
+  const cudaError_t ce = launch_kernel(e->fn, dim3(static_cast<unsigned>(grid)), dim3(plan.threads), args,
+                                       static_cast<size_t>(plan.smem_bytes), static_cast<cudaStream_t>(stream));
   if (ce != cudaSuccess) {
     (void)cudaGetLastError();
-    return cuda_fail("cudaLaunchKernel(dw_stream_kernel)", ce);
+    return cuda_fail("cudaLaunchKernelExC(dw_stream_kernel)", ce);
   }
   return DWB_OK;
 }

@@ -81,6 +81,16 @@ struct RingPos {
   }
 };
 
+// Programmatic dependent launch.  A kernel launched with the programmatic
+// stream-serialization attribute may start before the previous kernel of its
+// stream has finished; griddep_wait() returns once that kernel has completed
+// and its memory is visible, so every global read or write of data another
+// kernel may produce comes after it.  griddep_launch_dependents() lets the
+// next kernel of the stream start its own set-up early.  Both are no-ops for
+// a kernel launched without the attribute.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -221,6 +221,8 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
+    prefetch_tmap(&tmap_x);
+    prefetch_tmap(&tmap_w);
     for (int i = 0; i < RR; ++i) {
       mbar_init(&full_x[i], 1);
       mbar_init(&empty_x[i], p.consumer_warps);
@@ -236,6 +238,10 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
     fence_mbar_init();
   }
   __syncthreads();
+  // Everything above overlaps the previous kernel of the stream (programmatic
+  // dependent launch); from here on the kernel reads and writes global memory.
+  griddep_launch_dependents();
+  griddep_wait();
 
   if (warp == p.consumer_warps) {
     // ---------------- producer warp ----------------
@@ -243,8 +249,6 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
     // the input rows up to st + tile_h - 1 of every tile; a slot is refilled
     // only after the consumers released its previous use (empty barrier).
     if (lane == 0) {
-      prefetch_tmap(&tmap_x);
-      prefetch_tmap(&tmap_w);
       RingPos xr, wr;  // next slot to fill, and the parity of that fill
       long long xfills = 0, wfills = 0;
       bool ok = true;

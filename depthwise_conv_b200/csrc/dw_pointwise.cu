@@ -10,6 +10,7 @@
 
 #include "../../include/dwconv_b200.h"
 #include "dw_device.cuh"
+#include "dw_launch.h"
 
 namespace dwb {
 
@@ -18,6 +19,8 @@ __global__ void __launch_bounds__(256) bias_act_affine_kernel(const uint4* __res
                                                               const __half* __restrict__ scale,
                                                               const __half* __restrict__ shift, uint4* __restrict__ y,
                                                               long long groups, int cgroups) {
+  griddep_launch_dependents();
+  griddep_wait();  // x may be the previous kernel's output (programmatic dependent launch)
   for (long long g = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; g < groups;
        g += static_cast<long long>(gridDim.x) * blockDim.x) {
     const int c = static_cast<int>(g % cgroups) * 8;  // first of this vector's 8 channels
@@ -60,12 +63,15 @@ extern "C" int dwb_bias_act_affine_nhwc(const void* x, const void* bias, const v
   uint4* yv = static_cast<uint4*>(y);
   const __half *b = static_cast<const __half*>(bias), *sc = static_cast<const __half*>(scale),
                *sh = static_cast<const __half*>(shift);
-  const int cg = static_cast<int>(C / 8);
-  if (act == DWB_ACT_GELU)
-    bias_act_affine_kernel<kActGelu><<<blocks, 256, 0, s>>>(xv, b, sc, sh, yv, groups, cg);
-  else if (act == DWB_ACT_RELU)
-    bias_act_affine_kernel<kActRelu><<<blocks, 256, 0, s>>>(xv, b, sc, sh, yv, groups, cg);
-  else
-    bias_act_affine_kernel<kActNone><<<blocks, 256, 0, s>>>(xv, b, sc, sh, yv, groups, cg);
-  return cudaGetLastError() == cudaSuccess ? DWB_OK : DWB_ERR_CUDA;
+  int cg = static_cast<int>(C / 8);
+  long long ng = groups;
+  void* args[7] = {&xv, &b, &sc, &sh, &yv, &ng, &cg};
+  const void* fn = act == DWB_ACT_GELU   ? reinterpret_cast<const void*>(&bias_act_affine_kernel<kActGelu>)
+                   : act == DWB_ACT_RELU ? reinterpret_cast<const void*>(&bias_act_affine_kernel<kActRelu>)
+                                         : reinterpret_cast<const void*>(&bias_act_affine_kernel<kActNone>);
+  if (launch_kernel(fn, dim3(blocks), dim3(256), args, 0, s) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return DWB_ERR_CUDA;
+  }
+  return DWB_OK;
 }

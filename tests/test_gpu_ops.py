@@ -196,6 +196,36 @@ def test_cuda_graph_capture_of_c_abi(eng, oracle_mod):
     check(oracle_mod, y, exact2, "graph replay 2")
 
 
+def test_dependent_launch_chain_matches_synchronised_chain(eng):
+    """Kernels start early under programmatic dependent launch but read their inputs only after the
+    previous kernel has finished: a chain of dependent launches (each reading the previous output,
+    in place updates in between) equals the same chain with a device synchronisation between steps."""
+    torch.manual_seed(5)
+    C = 512
+    x0 = torch.randn(2, C, 20, 20, device="cuda").half().contiguous(memory_format=torch.channels_last)
+    ws = [(torch.randn(k, k, C, device="cuda") / k).half() for k in (7, 13, 27, 9)]
+    b = (torch.randn(C, device="cuda") * 0.1).half()
+    s = (torch.rand(C, device="cuda") + 0.5).half()
+
+    def chain(sync):
+        x = x0.clone()
+        for i in range(6):
+            w = ws[i % len(ws)]
+            y = eng.conv2d_nhwc_fused(x, w, b, s, None, x, "gelu")
+            if sync:
+                torch.cuda.synchronize()
+            eng.dw_ops.bias_act_affine(y, b, s, None, "relu", out=y)  # in place, read by the next launch
+            if sync:
+                torch.cuda.synchronize()
+            x = y
+        torch.cuda.synchronize()
+        return x
+
+    a, b2 = chain(False), chain(True)
+    assert torch.isfinite(a.float()).all()
+    assert torch.equal(a, b2)
+
+
 @pytest.mark.parametrize("act", ["none", "relu", "gelu"])
 def test_bias_act_affine(eng, act):
     """The pointwise-block epilogue: y = act(x + b) * s + t, against float64 math."""
