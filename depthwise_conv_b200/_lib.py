@@ -118,7 +118,7 @@ def load() -> ctypes.CDLL:
                 fn = getattr(lib, name)
                 fn.argtypes = argtypes
                 fn.restype = restype
-            if lib.dwb_abi_version() != 2:
+            if lib.dwb_abi_version() != 3:
                 raise RuntimeError("depthwise_conv_b200: ABI version mismatch")
             _lib = lib
     return _lib

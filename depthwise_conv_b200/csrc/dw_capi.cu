@@ -297,13 +297,12 @@ static int launch_plan(DeviceState* st, const dwb_plan& plan, const void* x, con
   p.slots = p.ncg * (plan.tile_h / plan.rows_per_thread);
   p.consumer_warps = plan.consumer_warps;
   if (p.consumer_warps != p.nsplit * p.slots) return DWB_ERR_BAD_ARG;
-  p.ring_rows = plan.ring_rows;
-  p.ring_wrows = plan.ring_wrows;
+  p.stages = plan.ring_rows;
   p.act = act;
-  p.x_ring_off = kBarrierBytes;
-  p.w_ring_off = kBarrierBytes + static_cast<uint32_t>(plan.ring_rows) * plan.tile_w_in * kPixelBytes;
+  p.ring_off = kBarrierBytes;
+  p.stage_bytes = static_cast<uint32_t>(plan.tile_w_in + K) * kPixelBytes;
   long long red_off = 0;
-  const long long smem_need = plan_smem_bytes(K, plan.tile_w_in, plan.ring_rows, plan.ring_wrows, p.nsplit, p.slots,
+  const long long smem_need = plan_smem_bytes(K, plan.tile_w_in, plan.ring_rows, p.nsplit, p.slots,
                                               plan.rows_per_thread, plan.cols_per_thread, &red_off);
   if (smem_need > plan.smem_bytes) return DWB_ERR_BAD_ARG;
   p.red_off = static_cast<uint32_t>(red_off);

@@ -11,8 +11,9 @@
 namespace dwb {
 
 // Error codes a kernel stores in the device error word (first writer wins)
-// when one of its bounded waits expires: 1 = input-row wait, 2 = weight-row
-// wait, 3 = ring-slot (empty) wait, 4 = row-split partial-sum hand-off.  The word lives in the launcher's
+// when one of its bounded waits expires: 1 = stage wait before a tile's
+// first step, 2 = stage wait of a step, 3 = producer's free-stage (empty)
+// wait, 4 = row-split partial-sum hand-off.  The word lives in the launcher's
 // translation unit; kernels receive its address.
 
 // ~1 s at 2 GHz: far above any legitimate wait (a row load takes ~1 us).
@@ -39,27 +40,41 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
-// Test the phase; if it is not complete the hardware suspends the thread
-// until it completes or kSuspendHintNs elapses (no spinning on issue slots).
+// Test the phase.  With SLEEP, a thread whose phase is not complete may be
+// suspended (up to kSuspendHintNs) instead of spinning on issue slots; the
+// consumers' waits use the plain form, whose wake-up follows the phase
+// completion more closely.
 constexpr uint32_t kSuspendHintNs = 1000000;  // 1 ms
+template <bool SLEEP>
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendHintNs)
-      : "memory");
+  if constexpr (SLEEP) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendHintNs)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+  }
   return ok != 0;
 }
 
 // Wait for the phase with the given parity to complete.  Returns false (and
 // records `code` in *err) if it has not completed within kWaitLimitCycles.
+template <bool SLEEP = false>
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err, int code) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_try_wait<SLEEP>(bar, parity)) return true;
   const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait<SLEEP>(bar, parity)) {
     if (clock64() - t0 > kWaitLimitCycles) {
       atomicCAS(err, 0, code);
       return false;
@@ -136,6 +151,20 @@ __device__ __forceinline__ void ffma2(f32x2& acc, f32x2 a, f32x2 b) {
 __device__ __forceinline__ void fadd2(f32x2& acc, f32x2 b) {
   asm("add.rn.f32x2 %0, %0, %1;" : "+l"(acc) : "l"(b));
 }
+__device__ __forceinline__ f32x2 fmul2(f32x2 a, f32x2 b) {
+  f32x2 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
+  f32x2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ f32x2 splat2(float v) {
+  const unsigned long long u = __float_as_uint(v);
+  return (u << 32) | u;
+}
 
 // half2 (two channels) -> packed fp32 pair.
 __device__ __forceinline__ f32x2 h2_to_f32x2(__half2 h) {
@@ -199,6 +228,25 @@ __device__ __forceinline__ float gelu_erf(float v) {
   const float ec = poly * ex2_approx(-a * a * 1.4426950408889634f);  // erfc(a)
   const float hv = 0.5f * v;
   return v >= 0.0f ? fmaf(-hv, ec, v) : hv * ec;  // v (1 - erfc/2)  |  v erfc / 2
+}
+
+// The same GELU on a packed pair: the polynomial and the products run as
+// fp32x2 instructions, only the reciprocal and the exponential per lane.
+__device__ __forceinline__ f32x2 gelu_erf2(f32x2 v) {
+  const f32x2 a = fmul2(v & 0x7fffffff7fffffffull, splat2(0.70710678118654752f));  // |v| / sqrt(2)
+  const float2 d = bits_f2(fma2(a, splat2(0.3275911f), splat2(1.0f)));
+  const f32x2 t = f2_bits(make_float2(rcp_approx(d.x), rcp_approx(d.y)));
+  f32x2 poly = fma2(splat2(1.061405429f), t, splat2(-1.453152027f));
+  poly = fma2(poly, t, splat2(1.421413741f));
+  poly = fma2(poly, t, splat2(-0.284496736f));
+  poly = fma2(poly, t, splat2(0.254829592f));
+  poly = fmul2(poly, t);
+  const float2 ea = bits_f2(fmul2(fmul2(a, a), splat2(-1.4426950408889634f)));
+  const f32x2 ec = fmul2(poly, f2_bits(make_float2(ex2_approx(ea.x), ex2_approx(ea.y))));  // erfc(a)
+  const f32x2 q = fmul2(fmul2(v, splat2(0.5f)), ec);  // v erfc / 2
+  const float2 pos = bits_f2(fma2(q, splat2(-1.0f), v));  // v (1 - erfc/2)
+  const float2 vf = bits_f2(v), qf = bits_f2(q);
+  return f2_bits(make_float2(vf.x >= 0.0f ? pos.x : qf.x, vf.y >= 0.0f ? pos.y : qf.y));
 }
 
 __device__ __forceinline__ float apply_act(float v, int act) {

@@ -16,9 +16,13 @@
 //   The kernel walks the kernel rows ki (step s).  At step s every output row
 //   h of the tile reads input row h - pad + s, so the tile needs the input
 //   rows [h0 - pad + s, h0 - pad + s + tile_h): a window that slides one row
-//   per step.  A dedicated producer warp streams those rows, and weight row
-//   ki, through two shared-memory rings guarded by full/empty mbarriers; the
-//   rings run continuously across the CTA's tiles:
+//   per step.  A dedicated producer warp streams the tile through a ring of
+//   shared-memory "stages" guarded by one full and one empty mbarrier each;
+//   the ring runs continuously across the CTA's tiles.  Stage q of a tile
+//   holds staged input row q and, for q >= tile_h - 1, weight row
+//   s_lo + q - (tile_h - 1) -- the weights of the step that first needs that
+//   input row -- so every step waits for exactly one stage and releases
+//   exactly one (stage st: its input row is never read again):
 //     input row  : [tile_w + K - 1 columns][64 channels] fp16 (zero padding
 //                  comes from TMA out-of-bounds fill)
 //     weight row : [K taps][64 channels] fp16
@@ -43,7 +47,7 @@
 //   adds them before the epilogue.  The hand-off is two mbarriers (partials
 //   written / area free again) with bounded waits, so a failing warp can
 //   never leave the others blocked.  Every warp still waits for and releases
-//   every ring slot in order, which keeps the ring protocol unchanged.
+//   every stage in order, which keeps the ring protocol unchanged.
 //
 // Epilogue (fused): v = acc + bias; v = act(v); v = v * scale + shift;
 //   v += residual; stored as half2, 128 contiguous bytes per warp.
@@ -57,6 +61,7 @@ constexpr int kChannelsPerCta = 64;                 // 32 lanes x 2 channels
 constexpr int kPixelBytes = kChannelsPerCta * 2;    // one staged pixel = 128 B
 constexpr int kPixelH2 = kChannelsPerCta / 2;       // half2 per staged pixel
 constexpr int kBarrierBytes = 1024;                 // mbarrier area at smem start
+constexpr bool kProducerSleeps = true;              // producer's empty-slot waits may suspend
 
 struct DwParams {
   __half* y;
@@ -72,9 +77,10 @@ struct DwParams {
   int consumer_warps;                // nsplit * slots
   int slots;                         // warps per split group (ncg * row groups)
   int nsplit;                        // row split S (1 = none)
-  int ring_rows, ring_wrows;
+  int stages;                       // stage ring depth
   int act;
-  uint32_t x_ring_off, w_ring_off;  // byte offsets inside dynamic smem
+  uint32_t ring_off;                // byte offset of stage 0 inside dynamic smem
+  uint32_t stage_bytes;             // (tile_w_in + K) staged pixels
   uint32_t red_off;                 // partial-sum exchange area (S > 1)
   int* err;                         // device error word (bounded-wait expiry)
 };
@@ -113,13 +119,15 @@ __device__ __forceinline__ TileInfo decode_tile(const DwParams& p, uint32_t t) {
 }
 
 // One kernel row for the warp's M rows (row m reads xrow[m]; rows whose
-// input row lies outside the image are skipped, warp-uniformly).
+// input row lies outside the image are skipped, warp-uniformly).  In mixed
+// mode the fp16 chains live only inside this call: each row's chains start at
+// zero and end in the fp32 accumulators before the next row.
 template <int K, int R, int M, int ACC>
-__device__ __forceinline__ void step_rows(f32x2 (&acc)[M][R], __half2 (&part)[M][(ACC == 1 && K >= 25) ? 2 : 1][R],
-                                          const __half2* __restrict__ wrow, const __half2* __restrict__ xrow0,
-                                          const __half2* __restrict__ xrow1, bool v0, bool v1) {
+__device__ __forceinline__ void step_rows(f32x2 (&acc)[M][R], const __half2* __restrict__ wrow,
+                                          const __half2* __restrict__ xrow0, const __half2* __restrict__ xrow1,
+                                          bool v0, bool v1) {
   constexpr int NJ = R + K - 1;
-  constexpr int SPLIT = (ACC == 1 && K >= 25) ? 2 : 1;
+  constexpr int SPLIT = (ACC == 1 && K >= 25) ? 2 : 1;  // chains of at most 16 taps
   if constexpr (ACC == 0) {
     f32x2 wv[K];
 #pragma unroll
@@ -147,6 +155,11 @@ __device__ __forceinline__ void step_rows(f32x2 (&acc)[M][R], __half2 (&part)[M]
     for (int m = 0; m < M; ++m) {
       if (m == 0 ? v0 : v1) {
         const __half2* xrow = m == 0 ? xrow0 : xrow1;
+        __half2 part[SPLIT][R];
+#pragma unroll
+        for (int c = 0; c < SPLIT; ++c)
+#pragma unroll
+          for (int r = 0; r < R; ++r) part[c][r] = __float2half2_rn(0.f);
 #pragma unroll
         for (int j = 0; j < NJ; ++j) {
           const __half2 xv = xrow[j * kPixelH2];
@@ -155,66 +168,73 @@ __device__ __forceinline__ void step_rows(f32x2 (&acc)[M][R], __half2 (&part)[M]
             const int kj = j - r;
             if (kj >= 0 && kj < K) {
               const int c = (SPLIT == 2 && kj >= K / 2 + 1) ? 1 : 0;
-              part[m][c][r] = __hfma2(xv, wv[kj], part[m][c][r]);
+              part[c][r] = __hfma2(xv, wv[kj], part[c][r]);
             }
           }
         }
+#pragma unroll
+        for (int c = 0; c < SPLIT; ++c)
+#pragma unroll
+          for (int r = 0; r < R; ++r) add_h2_to_f32x2(acc[m][r], part[c][r]);
       }
     }
   }
 }
 
 // Epilogue of one warp slot: y = act(acc) * scale + shift (+ residual), where
-// the accumulators already started from the bias.  ACT / RES are resolved
-// once per tile by the caller, so the loop is straight-line code.
-template <int ACT, bool RES, int M, int R>
+// the accumulators already started from the bias.  ACT / RES / FULL are
+// resolved once per tile by the caller, so the loop is straight-line code
+// (FULL: every row and column of the slot is inside the image).
+template <int ACT, bool RES, bool FULL, int M, int R>
 __device__ __forceinline__ void store_slot(const f32x2 (&acc)[M][R], f32x2 scale, f32x2 shift, __half2* y,
                                            const __half2* res, long long row_h2, int col_h2, int rows_valid,
                                            int cols_valid) {
 #pragma unroll
   for (int m = 0; m < M; ++m) {
-    if (m >= rows_valid) break;
+    if (!FULL && m >= rows_valid) break;
     __half2* yp = y + m * row_h2;
     const __half2* rp = RES ? res + m * row_h2 : nullptr;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-      if (r >= cols_valid) break;
-      float2 a = f32x2_unpack(acc[m][r]);
-      if (ACT != kActNone) {
-        a.x = apply_act(a.x, ACT);
-        a.y = apply_act(a.y, ACT);
+      if (!FULL && r >= cols_valid) break;
+      f32x2 a = acc[m][r];
+      if (ACT == kActGelu) {
+        a = gelu_erf2(a);
+      } else if (ACT == kActRelu) {
+        const float2 f = bits_f2(a);
+        a = f2_bits(make_float2(fmaxf(f.x, 0.0f), fmaxf(f.y, 0.0f)));
       }
-      f32x2 v = shift;
-      ffma2(v, f2_bits(a), scale);  // a * scale + shift, both channels in one FFMA2
-      float2 o = f32x2_unpack(v);
-      if (RES) {
-        const float2 rv = __half22float2(rp[r * col_h2]);
-        o.x += rv.x;
-        o.y += rv.y;
-      }
+      f32x2 v = fma2(a, scale, shift);  // a * scale + shift, both channels in one FFMA2
+      if (RES) fadd2(v, h2_to_f32x2(rp[r * col_h2]));
+      const float2 o = bits_f2(v);
       yp[r * col_h2] = __floats2half2_rn(o.x, o.y);
     }
   }
+}
+
+template <int ACT, bool RES, int M, int R>
+__device__ __forceinline__ void store_tile_slot(const f32x2 (&acc)[M][R], f32x2 scale, f32x2 shift, __half2* y,
+                                                const __half2* res, long long row_h2, int col_h2, int rows_valid,
+                                                int cols_valid) {
+  if (rows_valid == M && cols_valid == R)
+    store_slot<ACT, RES, true>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid);
+  else
+    store_slot<ACT, RES, false>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid);
 }
 
 template <int K, int R, int M, int ACC>
 __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                  const __grid_constant__ CUtensorMap tmap_w, const DwParams p) {
   constexpr int PAD = K / 2;
-  constexpr int SPLIT = (ACC == 1 && K >= 25) ? 2 : 1;
   extern __shared__ __align__(1024) unsigned char smem[];
 
-  const int RR = p.ring_rows;
-  const int RW = p.ring_wrows;
-  uint64_t* full_x = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty_x = full_x + RR;
-  uint64_t* full_w = empty_x + RR;
-  uint64_t* empty_w = full_w + RW;
-  uint64_t* red_full = empty_w + RW;   // row split: partial sums of a tile written
+  const int NS = p.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + NS;
+  uint64_t* red_full = empty + NS;     // row split: partial sums of a tile written
   uint64_t* red_empty = red_full + 1;  // row split: exchange area free again
-  unsigned char* xring = smem + p.x_ring_off;
-  unsigned char* wring = smem + p.w_ring_off;
-  const uint32_t row_bytes = static_cast<uint32_t>(p.tile_w_in) * kPixelBytes;
+  unsigned char* ring = smem + p.ring_off;
+  const uint32_t row_bytes = static_cast<uint32_t>(p.tile_w_in) * kPixelBytes;  // weight row follows it
   constexpr uint32_t wrow_bytes = K * kPixelBytes;
 
   const int warp = threadIdx.x >> 5;
@@ -223,13 +243,9 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
   if (threadIdx.x == 0) {
     prefetch_tmap(&tmap_x);
     prefetch_tmap(&tmap_w);
-    for (int i = 0; i < RR; ++i) {
-      mbar_init(&full_x[i], 1);
-      mbar_init(&empty_x[i], p.consumer_warps);
-    }
-    for (int i = 0; i < RW; ++i) {
-      mbar_init(&full_w[i], 1);
-      mbar_init(&empty_w[i], p.consumer_warps);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], p.consumer_warps);
     }
     if (p.nsplit > 1) {
       mbar_init(red_full, (p.nsplit - 1) * p.slots * 32);  // one arrival per thread of groups 1..S-1
@@ -245,38 +261,31 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
 
   if (warp == p.consumer_warps) {
     // ---------------- producer warp ----------------
-    // Issues, in the order the consumers need them, weight row s_lo+st and
-    // the input rows up to st + tile_h - 1 of every tile; a slot is refilled
-    // only after the consumers released its previous use (empty barrier).
+    // Fills the stages in order; a stage is refilled only after every
+    // consumer warp released its previous use (empty barrier).
     if (lane == 0) {
-      RingPos xr, wr;  // next slot to fill, and the parity of that fill
-      long long xfills = 0, wfills = 0;
+      RingPos fr;  // next stage to fill, and the parity of that fill
+      long long fills = 0;
       bool ok = true;
       for (uint32_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
         const TileInfo ti = decode_tile<K>(p, t);
-        int q = 0;  // next input row of this tile
-        for (int st = 0; st < ti.nsteps && ok; ++st) {
-          if (wfills >= RW) ok = mbar_wait_bounded(&empty_w[wr.slot], wr.phase ^ 1u, p.err, 3);
+        int abs_row = ti.h0 - PAD + ti.s_lo;  // input row of stage 0
+        for (int q = 0; q < ti.nrows; ++q, ++abs_row) {
+          if (fills >= NS) ok = mbar_wait_bounded<kProducerSleeps>(&empty[fr.slot], fr.phase ^ 1u, p.err, 3);
           if (!ok) break;
-          mbar_arrive_expect_tx(&full_w[wr.slot], wrow_bytes);
-          tma_load_3d(wring + wr.slot * wrow_bytes, &tmap_w, &full_w[wr.slot], ti.c0, 0, ti.s_lo + st);
-          wr.next(RW);
-          ++wfills;
-          const int need = (st + 1 == ti.nsteps) ? ti.nrows : st + p.tile_h;
-          for (; q < need; ++q) {
-            if (xfills >= RR) ok = mbar_wait_bounded(&empty_x[xr.slot], xr.phase ^ 1u, p.err, 3);
-            if (!ok) break;
-            const int abs_row = ti.h0 - PAD + ti.s_lo + q;
-            if (abs_row >= 0 && abs_row < p.H) {
-              mbar_arrive_expect_tx(&full_x[xr.slot], row_bytes);
-              tma_load_4d(xring + xr.slot * row_bytes, &tmap_x, &full_x[xr.slot], ti.c0, ti.w0 - PAD, abs_row,
-                          ti.b);
-            } else {
-              mbar_arrive(&full_x[xr.slot]);  // nothing to load: consumers skip this row
-            }
-            xr.next(RR);
-            ++xfills;
+          unsigned char* dst = ring + fr.slot * p.stage_bytes;
+          const bool xrow = abs_row >= 0 && abs_row < p.H;
+          const bool wrow = q >= p.tile_h - 1;
+          const uint32_t bytes = (xrow ? row_bytes : 0u) + (wrow ? wrow_bytes : 0u);
+          if (bytes) {
+            mbar_arrive_expect_tx(&full[fr.slot], bytes);
+            if (xrow) tma_load_4d(dst, &tmap_x, &full[fr.slot], ti.c0, ti.w0 - PAD, abs_row, ti.b);
+            if (wrow) tma_load_3d(dst + row_bytes, &tmap_w, &full[fr.slot], ti.c0, 0, ti.s_lo + q - (p.tile_h - 1));
+          } else {
+            mbar_arrive(&full[fr.slot]);  // nothing to load (rows above/below the image are skipped)
           }
+          fr.next(NS);
+          ++fills;
         }
       }
     }
@@ -292,9 +301,8 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
   const int col0 = cg * R;   // first tile column of this warp
   const int xoff = col0 * kPixelH2 + lane;  // half2 offset of this thread's first input column
 
-  RingPos wait_x;  // next input row to wait for
-  RingPos wait_w;  // weight row of the current step
-  RingPos rel_x;   // next input row to release
+  RingPos wait_s;  // next stage to wait for
+  RingPos rel_s;   // next stage to release (stage st of the current tile during step st)
   bool ok = true;
 
   f32x2 bias = 0, scale = 0, shift = 0;
@@ -325,41 +333,32 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
     for (int m = 0; m < M; ++m)
 #pragma unroll
       for (int r = 0; r < R; ++r) acc[m][r] = acc0;
-    __half2 part[M][SPLIT][R];  // mixed mode fp16 chains (unused in fp32 mode)
-#pragma unroll
-    for (int m = 0; m < M; ++m)
-#pragma unroll
-      for (int c = 0; c < SPLIT; ++c)
-#pragma unroll
-        for (int r = 0; r < R; ++r) part[m][c][r] = __float2half2_rn(0.f);
     int turn = sg;  // steps until this warp's next kernel row
 
     // warps whose columns all lie right of the image have nothing to compute
     const bool any_col = ti.w0 + col0 < p.W;
 
-    // slot of row trow0 of this tile (row 0 of the tile is at rel_x)
-    int my_slot = rel_x.slot + trow0;
-    if (my_slot >= RR) my_slot -= RR;
+    // stage of row trow0 of this tile (stage 0 of the tile is at rel_s)
+    int my_slot = rel_s.slot + trow0;
+    if (my_slot >= NS) my_slot -= NS;
 
-    // Rows [0, tile_h) are needed by step 0.
-    for (int q = 0; q < min(p.tile_h, ti.nrows) && ok; ++q) {
-      ok = mbar_wait_bounded(&full_x[wait_x.slot], wait_x.phase, p.err, 1);
-      wait_x.next(RR);
+    // Stages [0, tile_h - 1) hold input rows that step 0 needs as well.
+    for (int q = 0; q < p.tile_h - 1 && ok; ++q) {
+      ok = mbar_wait_bounded(&full[wait_s.slot], wait_s.phase, p.err, 1);
+      wait_s.next(NS);
     }
 
     for (int st = 0; st < ti.nsteps && ok; ++st) {
-      if (st > 0 && st + p.tile_h - 1 < ti.nrows) {  // row st + tile_h - 1 arrives for this step
-        ok = mbar_wait_bounded(&full_x[wait_x.slot], wait_x.phase, p.err, 1);
-        wait_x.next(RR);
-      }
-      if (ok) ok = mbar_wait_bounded(&full_w[wait_w.slot], wait_w.phase, p.err, 2);
+      // stage st + tile_h - 1: the last input row and the weight row of this step
+      ok = mbar_wait_bounded(&full[wait_s.slot], wait_s.phase, p.err, 2);
       if (!ok) break;
+      const __half2* wrow = reinterpret_cast<const __half2*>(ring + wait_s.slot * p.stage_bytes + row_bytes) + lane;
+      wait_s.next(NS);
 
       const int s = ti.s_lo + st;  // kernel row
-      const __half2* wrow = reinterpret_cast<const __half2*>(wring + wait_w.slot * wrow_bytes) + lane;
-      const int slot1 = (my_slot + 1 == RR) ? 0 : my_slot + 1;
-      const __half2* xrow0 = reinterpret_cast<const __half2*>(xring + my_slot * row_bytes) + xoff;
-      const __half2* xrow1 = reinterpret_cast<const __half2*>(xring + slot1 * row_bytes) + xoff;
+      const int slot1 = (my_slot + 1 == NS) ? 0 : my_slot + 1;
+      const __half2* xrow0 = reinterpret_cast<const __half2*>(ring + my_slot * p.stage_bytes) + xoff;
+      const __half2* xrow1 = reinterpret_cast<const __half2*>(ring + slot1 * p.stage_bytes) + xoff;
       const int out0 = ti.h0 + trow0;
       const int in0 = out0 - PAD + s;
       const bool mine = turn == 0;  // warp-uniform
@@ -368,35 +367,20 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
       const bool v1 = mine && any_col && M == 2 && out0 + 1 < p.H && in0 + 1 >= 0 && in0 + 1 < p.H;  // warp-uniform
 
       if (v0 || v1) {
-        step_rows<K, R, M, ACC>(acc, part, wrow, xrow0, xrow1, v0, v1);
-        if constexpr (ACC == 1) {  // the fp16 chains of this kernel row end here
-#pragma unroll
-          for (int m = 0; m < M; ++m)
-#pragma unroll
-            for (int c = 0; c < SPLIT; ++c)
-#pragma unroll
-              for (int r = 0; r < R; ++r) {
-                add_h2_to_f32x2(acc[m][r], part[m][c][r]);
-                part[m][c][r] = __float2half2_rn(0.f);
-              }
-        }
+        step_rows<K, R, M, ACC>(acc, wrow, xrow0, xrow1, v0, v1);
       }
 
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&empty_x[rel_x.slot]);  // row st of the tile is never read again
-        mbar_arrive(&empty_w[wait_w.slot]);
-      }
-      rel_x.next(RR);
-      wait_w.next(RW);
+      if (lane == 0) mbar_arrive(&empty[rel_s.slot]);  // input row st of the tile is never read again
+      rel_s.next(NS);
       my_slot = slot1;
     }
     if (!ok) break;
-    // The last tile_h - 1 rows of the tile are done too.
+    // The last tile_h - 1 stages of the tile are done too.
     __syncwarp();
     for (int q = ti.nsteps; q < ti.nrows; ++q) {
-      if (lane == 0) mbar_arrive(&empty_x[rel_x.slot]);
-      rel_x.next(RR);
+      if (lane == 0) mbar_arrive(&empty[rel_s.slot]);
+      rel_s.next(NS);
     }
 
     // ---------------- row split: partial sums to group 0 ----------------
@@ -441,12 +425,12 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
       const long long row_h2 = static_cast<long long>(p.W) * p.C / 2;
       const int col_h2 = p.C / 2;
       switch (p.act * 2 + (res != nullptr)) {  // one branch per tile, then straight-line stores
-        case 0: store_slot<kActNone, false>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
-        case 1: store_slot<kActNone, true>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
-        case 2: store_slot<kActRelu, false>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
-        case 3: store_slot<kActRelu, true>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
-        case 4: store_slot<kActGelu, false>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
-        default: store_slot<kActGelu, true>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
+        case 0: store_tile_slot<kActNone, false>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
+        case 1: store_tile_slot<kActNone, true>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
+        case 2: store_tile_slot<kActRelu, false>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
+        case 3: store_tile_slot<kActRelu, true>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
+        case 4: store_tile_slot<kActGelu, false>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
+        default: store_tile_slot<kActGelu, true>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
       }
     }
   }

@@ -67,16 +67,14 @@ int estimate_regs(int K, int R, int M, int acc) {
   return std::min(255, std::max(48, est));
 }
 
-long long plan_smem_bytes(int K, int tile_w_in, int ring_rows, int ring_wrows, int nsplit, int slots, int M, int R,
-                          long long* red_off) {
-  long long off = kBarrierBytes + static_cast<long long>(ring_rows) * tile_w_in * kPixelBytes +
-                  static_cast<long long>(ring_wrows) * K * kPixelBytes;
+long long plan_smem_bytes(int K, int tile_w_in, int stages, int nsplit, int slots, int M, int R, long long* red_off) {
+  long long off = kBarrierBytes + static_cast<long long>(stages) * (tile_w_in + K) * kPixelBytes;
   if (red_off) *red_off = off;
   if (nsplit > 1) off += static_cast<long long>(nsplit - 1) * slots * M * R * 32 * 8;
   return off;
 }
 
-bool barriers_fit(int ring_rows, int ring_wrows) { return (2 * (ring_rows + ring_wrows) + 2) * 8 <= kBarrierBytes; }
+bool barriers_fit(int stages) { return (2 * stages + 2) * 8 <= kBarrierBytes; }
 
 int validate_problem(const dwb_problem& pr) {
   const long long B = pr.batch, H = pr.height, W = pr.width, C = pr.channels;
@@ -158,19 +156,17 @@ int enumerate_plans(const dwb_problem& pr, const HwInfo& hw, RegsFn regs, void* 
 
           // Prefetch depth (rows the producer may run ahead of the consumers):
           // deeper rings hide the load latency, shallower ones fit more CTAs.
-          // A row split keeps S steps in flight, so its rings are S - 1 rows deeper.
+          // A row split keeps S steps in flight, so its ring is S - 1 stages deeper.
           int last_ring = -1;
           const int depths[4] = {2, 4, 8, K + 64};
           for (int di = 0; di < 4; ++di) {
             const int ring_rows = std::min(tile_h + nsplit - 1 + depths[di], tile_h + K - 1);
             if (ring_rows == last_ring) continue;
             last_ring = ring_rows;
-            const int ring_wrows = std::min(std::max(3, nsplit + depths[di]), K);
             long long red_off = 0;
-            const long long smem =
-                plan_smem_bytes(K, tile_w_in, ring_rows, ring_wrows, nsplit, slots, M, R, &red_off);
+            const long long smem = plan_smem_bytes(K, tile_w_in, ring_rows, nsplit, slots, M, R, &red_off);
             if (smem > hw.smem_optin) break;
-            if (!barriers_fit(ring_rows, ring_wrows)) break;
+            if (!barriers_fit(ring_rows)) break;
             const int cps = static_cast<int>(std::min<long long>(
                 {hw.smem_per_sm / (smem + hw.smem_reserved), static_cast<long long>(cps_regs),
                  hw.max_threads_sm / threads, hw.max_ctas_sm}));
@@ -202,7 +198,7 @@ int enumerate_plans(const dwb_problem& pr, const HwInfo& hw, RegsFn regs, void* 
           pl.tile_w = tile_w;
           pl.tile_w_in = tile_w_in;
           pl.ring_rows = ring_rows;
-          pl.ring_wrows = ring_wrows;
+          pl.ring_wrows = 0;
           pl.consumer_warps = consumer_warps;
           pl.threads = threads;
           pl.smem_bytes = static_cast<int32_t>(smem);
@@ -265,14 +261,15 @@ int check_plan(const dwb_problem& pr, const HwInfo& hw, int regs, dwb_plan* p) {
   const int slots = (p->tile_w / R) * (p->tile_h / M);
   const int cw = S * slots;
   if (slots < 1 || cw > 31) return DWB_ERR_BAD_ARG;
-  if (p->ring_rows < p->tile_h || p->ring_wrows < 1 || p->ring_wrows > K) return DWB_ERR_BAD_ARG;
-  if (!barriers_fit(p->ring_rows, p->ring_wrows)) return DWB_ERR_BAD_ARG;
+  if (p->ring_rows < p->tile_h) return DWB_ERR_BAD_ARG;
+  if (!barriers_fit(p->ring_rows)) return DWB_ERR_BAD_ARG;
+  p->ring_wrows = 0;  // weight rows travel in the input-row stages
   p->channel_block = kChannelsPerCta;
   p->tile_w_in = p->tile_w + K - 1;
   p->consumer_warps = cw;
   p->threads = 32 * (cw + 1);
   p->reserved0 = 0;
-  const long long smem = plan_smem_bytes(K, p->tile_w_in, p->ring_rows, p->ring_wrows, S, slots, M, R, nullptr);
+  const long long smem = plan_smem_bytes(K, p->tile_w_in, p->ring_rows, S, slots, M, R, nullptr);
   if (smem > hw.smem_optin) return DWB_ERR_BAD_ARG;
   if (regs > 0 && ctas_by_registers(regs, cw + 1, hw.regs_per_sm) < 1) return DWB_ERR_BAD_ARG;
   p->smem_bytes = static_cast<int32_t>(smem);

@@ -34,14 +34,14 @@ extern const int kVariantR[kNumVariantR];
 extern const int kVariantM[2];
 bool variant_compiled(int K, int R, int M, int acc);
 
-// Dynamic shared memory of a plan: mbarriers, input-row ring, weight-row
-// ring, then (row split S > 1) the partial-sum exchange area of groups
-// 1..S-1.  *red_off receives the exchange area's byte offset.
-long long plan_smem_bytes(int K, int tile_w_in, int ring_rows, int ring_wrows, int nsplit, int slots, int M, int R,
-                          long long* red_off);
+// Dynamic shared memory of a plan: mbarriers, the stage ring (each stage =
+// one staged input row of tile_w_in pixels + one weight row of K taps), then
+// (row split S > 1) the partial-sum exchange area of groups 1..S-1.
+// *red_off receives the exchange area's byte offset.
+long long plan_smem_bytes(int K, int tile_w_in, int stages, int nsplit, int slots, int M, int R, long long* red_off);
 
-// Largest ring depth the 1 KB mbarrier area holds: 2 * (ring_rows + ring_wrows) + 2 barriers.
-bool barriers_fit(int ring_rows, int ring_wrows);
+// Whether the 1 KB mbarrier area holds the ring's 2 * stages + 2 barriers.
+bool barriers_fit(int stages);
 
 // Range checks shared by every entry point.  Returns a dwb_status.
 int validate_problem(const dwb_problem& pr);

@@ -28,14 +28,19 @@ __global__ void __launch_bounds__(256) bias_act_affine_kernel(const uint4* __res
     __half2* h = reinterpret_cast<__half2*>(&v);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      float2 f = __half22float2(h[i]);
       const int ci = c + 2 * i;
-      const float2 b = bias ? __half22float2(*reinterpret_cast<const __half2*>(bias + ci)) : make_float2(0.f, 0.f);
-      const float2 s = scale ? __half22float2(*reinterpret_cast<const __half2*>(scale + ci)) : make_float2(1.f, 1.f);
-      const float2 t = shift ? __half22float2(*reinterpret_cast<const __half2*>(shift + ci)) : make_float2(0.f, 0.f);
-      f.x = fmaf(apply_act(f.x + b.x, ACT), s.x, t.x);
-      f.y = fmaf(apply_act(f.y + b.y, ACT), s.y, t.y);
-      h[i] = __floats2half2_rn(f.x, f.y);
+      f32x2 v = h2_to_f32x2(h[i]);
+      if (bias) fadd2(v, h2_to_f32x2(*reinterpret_cast<const __half2*>(bias + ci)));
+      if (ACT == kActGelu) {
+        v = gelu_erf2(v);
+      } else if (ACT == kActRelu) {
+        const float2 f = bits_f2(v);
+        v = f2_bits(make_float2(fmaxf(f.x, 0.0f), fmaxf(f.y, 0.0f)));
+      }
+      const f32x2 s = scale ? h2_to_f32x2(*reinterpret_cast<const __half2*>(scale + ci)) : splat2(1.0f);
+      const f32x2 t = shift ? h2_to_f32x2(*reinterpret_cast<const __half2*>(shift + ci)) : splat2(0.0f);
+      const float2 o = bits_f2(fma2(v, s, t));
+      h[i] = __floats2half2_rn(o.x, o.y);
     }
     y[g] = v;
   }

@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define DWB_ABI_VERSION 2
+#define DWB_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define DWB_API __attribute__((visibility("default")))
@@ -82,8 +82,9 @@ typedef struct dwb_plan {
     int32_t channel_block;      /* CB: channels per CTA (2 per lane)            */
     int32_t tile_h, tile_w;     /* output tile per CTA                          */
     int32_t tile_w_in;          /* input columns staged per row (tile_w + K-1)  */
-    int32_t ring_rows;          /* input-row ring slots                         */
-    int32_t ring_wrows;         /* weight-row ring slots                        */
+    int32_t ring_rows;          /* stage ring slots (one input row + one weight
+                                   row each); at least tile_h                   */
+    int32_t ring_wrows;         /* unused, 0                                    */
     int32_t consumer_warps;
     int32_t threads;
     int32_t smem_bytes;

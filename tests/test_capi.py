@@ -39,7 +39,7 @@ def test_every_declared_symbol_is_exported_and_bound(lib):
 
 def test_abi_version_and_status_strings(lib):
     from depthwise_conv_b200 import _lib
-    assert lib.dwb_abi_version() == 2
+    assert lib.dwb_abi_version() == 3
     for code in range(9):
         assert lib.dwb_status_string(code) and b"unknown" not in lib.dwb_status_string(code)
     assert lib.dwb_status_string(99) == b"unknown status"
@@ -109,9 +109,9 @@ def test_plans_respect_hardware_limits(B, H, W, C, K, accum):
     per_warp = -(-p["regs_estimate"] * 32 // 256) * 256
     assert -(-(p["consumer_warps"] + 1) // 4) * per_warp <= 16384
     assert p["smem_bytes"] <= 232448 and p["ctas_per_sm"] >= 1
-    assert p["ring_rows"] >= p["tile_h"] and p["ring_wrows"] >= 1
-    assert (2 * (p["ring_rows"] + p["ring_wrows"]) + 2) * 8 <= 1024  # mbarrier area
-    ring = 1024 + p["ring_rows"] * p["tile_w_in"] * 128 + p["ring_wrows"] * K * 128
+    assert p["ring_rows"] >= p["tile_h"] and p["ring_wrows"] == 0
+    assert (2 * p["ring_rows"] + 2) * 8 <= 1024  # mbarrier area
+    ring = 1024 + p["ring_rows"] * (p["tile_w_in"] + K) * 128  # stages: an input row and a weight row each
     slots = p["consumer_warps"] // S
     assert p["smem_bytes"] == ring + (S - 1) * slots * M * R * 32 * 8  # + partial-sum exchange area
     tiles = -(-H // p["tile_h"]) * -(-W // p["tile_w"]) * -(-C // 64)
