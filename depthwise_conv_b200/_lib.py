@@ -46,7 +46,7 @@ class Plan(ctypes.Structure):
                 ("ring_rows", ctypes.c_int32), ("ring_wrows", ctypes.c_int32), ("consumer_warps", ctypes.c_int32),
                 ("threads", ctypes.c_int32), ("smem_bytes", ctypes.c_int32), ("ctas_per_sm", ctypes.c_int32),
                 ("grid", ctypes.c_int64), ("tiles", ctypes.c_int64), ("accum", ctypes.c_int32), ("regs_estimate", ctypes.c_int32),
-                ("model_cost", ctypes.c_double), ("row_splits", ctypes.c_int32), ("reserved0", ctypes.c_int32)]
+                ("model_cost", ctypes.c_double), ("row_splits", ctypes.c_int32), ("load_schedule", ctypes.c_int32)]
 
     def as_dict(self) -> dict:
         return {name: getattr(self, name) for name, _ in self._fields_}
@@ -118,7 +118,7 @@ def load() -> ctypes.CDLL:
                 fn = getattr(lib, name)
                 fn.argtypes = argtypes
                 fn.restype = restype
-            if lib.dwb_abi_version() != 3:
+            if lib.dwb_abi_version() != 4:
                 raise RuntimeError("depthwise_conv_b200: ABI version mismatch")
             _lib = lib
     return _lib

@@ -57,11 +57,11 @@ int kernels_for_k(int K, const KernelEntry** out) {
   }
 }
 
-static const KernelEntry* find_variant(int K, int R, int M, int acc) {
+static const KernelEntry* find_variant(int K, int R, int M, int acc, int pre) {
   const KernelEntry* tab = nullptr;
   const int n = kernels_for_k(K, &tab);
   for (int i = 0; i < n; ++i)
-    if (tab[i].r == R && tab[i].m == M && tab[i].acc == acc) return &tab[i];
+    if (tab[i].r == R && tab[i].m == M && tab[i].acc == acc && tab[i].pre == pre) return &tab[i];
   return nullptr;
 }
 
@@ -70,7 +70,7 @@ static const KernelEntry* find_variant(int K, int R, int M, int acc) {
 static __device__ int g_device_error;
 
 constexpr int kMaxDevices = 64;
-constexpr int kMaxVariants = 16 * kNumVariantR * 4;  // K values x R x M x accum
+constexpr int kMaxVariants = 16 * kNumVariantR * 8;  // K values x R x M x accum x load schedule
 
 struct VariantState {
   int regs = -1;         // -1 unknown, 0 unavailable
@@ -107,12 +107,12 @@ static int driver_fail(const char* what, int code) {
 
 static DeviceState g_devices[kMaxDevices];
 
-static int variant_slot(int K, int R, int M, int acc) {
+static int variant_slot(int K, int R, int M, int acc, int pre) {
   int ri = 0;
   for (; ri < kNumVariantR - 1; ++ri)
     if (kVariantR[ri] == R) break;
   const int mi = (M == 2) ? 0 : 1;
-  return ((K / 2) * kNumVariantR + ri) * 4 + mi * 2 + acc;
+  return ((K / 2) * kNumVariantR + ri) * 8 + mi * 4 + acc * 2 + (pre ? 1 : 0);
 }
 
 static void init_device(int dev, DeviceState* st) {
@@ -159,11 +159,11 @@ static int get_device_state(DeviceState** out) {
   return st->status;
 }
 
-static int regs_of_variant(int K, int R, int M, int acc, void* ctx) {
+static int regs_of_variant(int K, int R, int M, int acc, int pre, void* ctx) {
   DeviceState* st = static_cast<DeviceState*>(ctx);
-  const KernelEntry* e = find_variant(K, R, M, acc);
+  const KernelEntry* e = find_variant(K, R, M, acc, pre);
   if (!e) return 0;
-  VariantState& vs = st->variants[variant_slot(K, R, M, acc)];
+  VariantState& vs = st->variants[variant_slot(K, R, M, acc, pre)];
   std::lock_guard<std::mutex> lk(st->mu);
   if (vs.regs < 0) {
     cudaFuncAttributes fa;
@@ -173,7 +173,7 @@ static int regs_of_variant(int K, int R, int M, int acc, void* ctx) {
 }
 
 static int ensure_smem_attr(DeviceState* st, const KernelEntry* e, int smem) {
-  VariantState& vs = st->variants[variant_slot(e->k, e->r, e->m, e->acc)];
+  VariantState& vs = st->variants[variant_slot(e->k, e->r, e->m, e->acc, e->pre)];
   std::lock_guard<std::mutex> lk(st->mu);
   if (vs.smem_max >= smem) return DWB_OK;
   const cudaError_t ce = cudaFuncSetAttribute(e->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -263,7 +263,7 @@ static dwb_problem make_problem(long long B, long long H, long long W, long long
 static int launch_plan(DeviceState* st, const dwb_plan& plan, const void* x, const void* w, const void* bias,
                        const void* scale, const void* shift, const void* residual, void* y, long long B, long long H,
                        long long W, long long C, int K, int act, void* stream) {
-  const KernelEntry* e = find_variant(K, plan.cols_per_thread, plan.rows_per_thread, plan.accum);
+  const KernelEntry* e = find_variant(K, plan.cols_per_thread, plan.rows_per_thread, plan.accum, plan.load_schedule);
   if (!e) return DWB_ERR_UNSUPPORTED;
   int rc = ensure_smem_attr(st, e, plan.smem_bytes);
   if (rc != DWB_OK) return rc;
@@ -313,7 +313,7 @@ static int launch_plan(DeviceState* st, const dwb_plan& plan, const void* x, con
   // count (one tile per CTA when it equals the tile count).
   long long grid = plan.grid;
   {
-    VariantState& vs = st->variants[variant_slot(e->k, e->r, e->m, e->acc)];
+    VariantState& vs = st->variants[variant_slot(e->k, e->r, e->m, e->acc, e->pre)];
     std::lock_guard<std::mutex> lk(st->mu);
     if (vs.occ_threads != plan.threads || vs.occ_smem != plan.smem_bytes) {
       int occ = 0;
@@ -348,6 +348,7 @@ struct TunedPlan {
   long long B, H, W, C;
   int K, accum, R, M, tile_h, tile_w, ring_rows, ring_wrows, grid;
   int splits;  // row split (0 or 1 = none)
+  int pre;     // load schedule
 };
 static const TunedPlan kTunedPlans[] = {
 #include "dw_tuned_plans.inc"
@@ -378,7 +379,8 @@ static bool tuned_plan(DeviceState* st, const dwb_problem& pr, dwb_plan* out) {
   p.ring_wrows = best->ring_wrows;
   p.grid = best->grid;
   p.row_splits = best->splits;
-  const int regs = regs_of_variant(p.kernel_size, p.cols_per_thread, p.rows_per_thread, p.accum, st);
+  p.load_schedule = best->pre;
+  const int regs = regs_of_variant(p.kernel_size, p.cols_per_thread, p.rows_per_thread, p.accum, p.load_schedule, st);
   if (regs <= 0 || check_plan(pr, st->hw, regs, &p) != DWB_OK) return false;
   p.ctas_per_sm = 0;  // not modelled for tuned plans
   *out = p;
@@ -506,7 +508,7 @@ int dwb_conv2d_nhwc_fwd_planned(const void* x, const void* w, const void* bias, 
   rc = get_device_state(&st);
   if (rc != DWB_OK) return rc;
   dwb_plan p = *plan;
-  const int regs = regs_of_variant(K, p.cols_per_thread, p.rows_per_thread, p.accum, st);
+  const int regs = regs_of_variant(K, p.cols_per_thread, p.rows_per_thread, p.accum, p.load_schedule, st);
   if (regs <= 0) return DWB_ERR_UNSUPPORTED;
   rc = check_plan(make_problem(B, H, W, C, K, p.accum), st->hw, regs, &p);
   if (rc != DWB_OK) return rc;

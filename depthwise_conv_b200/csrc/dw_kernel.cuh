@@ -28,6 +28,12 @@
 //     weight row : [K taps][64 channels] fp16
 //   Kernel rows whose input rows all fall outside the image are skipped.
 //
+// Load schedule (PRE): 0 = each input column is read from shared memory
+//   right before the FMAs that use it; 1 = the warp first reads its whole
+//   input row segment into registers, then runs the FMAs.  The two compile to
+//   different instruction schedules; which is faster depends on K, R and M,
+//   so both are compiled for the mixed mode and the planner/tuner picks.
+//
 // Inner loop (weight-stationary per kernel row)
 //   The K weights of row ki are held in registers; then the thread slides
 //   along R + K - 1 input columns of its M rows at once (the rows are
@@ -122,7 +128,7 @@ __device__ __forceinline__ TileInfo decode_tile(const DwParams& p, uint32_t t) {
 // input row lies outside the image are skipped, warp-uniformly).  In mixed
 // mode the fp16 chains live only inside this call: each row's chains start at
 // zero and end in the fp32 accumulators before the next row.
-template <int K, int R, int M, int ACC>
+template <int K, int R, int M, int ACC, int PRE>
 __device__ __forceinline__ void step_rows(f32x2 (&acc)[M][R], const __half2* __restrict__ wrow,
                                           const __half2* __restrict__ xrow0, const __half2* __restrict__ xrow1,
                                           bool v0, bool v1) {
@@ -160,9 +166,19 @@ __device__ __forceinline__ void step_rows(f32x2 (&acc)[M][R], const __half2* __r
         for (int c = 0; c < SPLIT; ++c)
 #pragma unroll
           for (int r = 0; r < R; ++r) part[c][r] = __float2half2_rn(0.f);
+        __half2 xs[PRE ? NJ : 1];
+        if constexpr (PRE) {
+#pragma unroll
+          for (int j = 0; j < NJ; ++j) xs[j] = xrow[j * kPixelH2];
+        }
 #pragma unroll
         for (int j = 0; j < NJ; ++j) {
-          const __half2 xv = xrow[j * kPixelH2];
+          __half2 xv;
+          if constexpr (PRE) {
+            xv = xs[j];
+          } else {
+            xv = xrow[j * kPixelH2];
+          }
 #pragma unroll
           for (int r = 0; r < R; ++r) {
             const int kj = j - r;
@@ -222,7 +238,7 @@ __device__ __forceinline__ void store_tile_slot(const f32x2 (&acc)[M][R], f32x2 
     store_slot<ACT, RES, false>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid);
 }
 
-template <int K, int R, int M, int ACC>
+template <int K, int R, int M, int ACC, int PRE>
 __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                  const __grid_constant__ CUtensorMap tmap_w, const DwParams p) {
   constexpr int PAD = K / 2;
@@ -367,7 +383,7 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
       const bool v1 = mine && any_col && M == 2 && out0 + 1 < p.H && in0 + 1 >= 0 && in0 + 1 < p.H;  // warp-uniform
 
       if (v0 || v1) {
-        step_rows<K, R, M, ACC>(acc, wrow, xrow0, xrow1, v0, v1);
+        step_rows<K, R, M, ACC, PRE>(acc, wrow, xrow0, xrow1, v0, v1);
       }
 
       __syncwarp();
@@ -438,7 +454,7 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
 
 // One compiled variant of the kernel, registered for the launcher.
 struct KernelEntry {
-  int k, r, m, acc;
+  int k, r, m, acc, pre;
   const void* fn;
 };
 

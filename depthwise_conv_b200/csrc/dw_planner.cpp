@@ -21,13 +21,22 @@ namespace dwb {
 
 const int kVariantR[kNumVariantR] = {32, 28, 16, 14, 8, 7};
 
-bool variant_compiled(int K, int R, int M, int acc) {
-  (void)acc;
+bool variant_compiled(int K, int R, int M, int acc, int pre) {
   if (M != 1 && M != 2) return false;
+  if (pre != 0 && !(pre == 1 && acc == DWB_ACCUM_MIXED)) return false;
   if (R == 7 || R == 8 || R == 14 || R == 16) return true;
   return (R == 28 || R == 32) && K <= 13;
 }
 const int kVariantM[2] = {2, 1};
+
+int default_load_schedule(int K, int R, int M, int acc) {
+  (void)R;
+  (void)M;
+  // measured on B200: reading the row up front wins for the smallest and the
+  // middle kernel sizes, the interleaved schedule for K = 9..13 and K >= 29
+  if (acc != DWB_ACCUM_MIXED) return 0;
+  return (K <= 7 || (K >= 15 && K <= 27)) ? 1 : 0;
+}
 
 namespace {
 constexpr int kChannelsPerCta = 64;
@@ -100,8 +109,9 @@ int enumerate_plans(const dwb_problem& pr, const HwInfo& hw, RegsFn regs, void* 
     const int R = kVariantR[ri];
     for (int mi = 0; mi < 2; ++mi) {
       const int M = kVariantM[mi];
-      if (!variant_compiled(K, R, M, pr.accum)) continue;
-      const int rg = regs ? regs(K, R, M, pr.accum, ctx) : estimate_regs(K, R, M, pr.accum);
+      const int pre = default_load_schedule(K, R, M, pr.accum);
+      if (!variant_compiled(K, R, M, pr.accum, pre)) continue;
+      const int rg = regs ? regs(K, R, M, pr.accum, pre, ctx) : estimate_regs(K, R, M, pr.accum);
       if (rg <= 0) continue;  // variant not compiled
       const int ncg_box = (kMaxBoxDim - (K - 1)) / R;
       const int ncg_need = static_cast<int>(ceil_div(std::min<long long>(W, 8LL * R), R));
@@ -209,6 +219,7 @@ int enumerate_plans(const dwb_problem& pr, const HwInfo& hw, RegsFn regs, void* 
           pl.regs_estimate = rg;
           pl.model_cost = cost;
           pl.row_splits = nsplit;
+          pl.load_schedule = pre;
           ++count;
           if (sink) sink(pl, sink_ctx);
           }
@@ -252,7 +263,8 @@ int check_plan(const dwb_problem& pr, const HwInfo& hw, int regs, dwb_plan* p) {
   if (vst != DWB_OK) return vst;
   const int K = pr.kernel_size;
   const int R = p->cols_per_thread, M = p->rows_per_thread;
-  if (!variant_compiled(K, R, M, p->accum) || p->kernel_size != K || p->accum != pr.accum) return DWB_ERR_BAD_ARG;
+  if (!variant_compiled(K, R, M, p->accum, p->load_schedule) || p->kernel_size != K || p->accum != pr.accum)
+    return DWB_ERR_BAD_ARG;
   if (p->tile_w < R || p->tile_w % R != 0 || p->tile_h < M || p->tile_h % M != 0) return DWB_ERR_BAD_ARG;
   if (p->tile_w + K - 1 > kMaxBoxDim) return DWB_ERR_BAD_ARG;
   if (p->row_splits == 0) p->row_splits = 1;  // plans from callers that predate the field
@@ -268,7 +280,6 @@ int check_plan(const dwb_problem& pr, const HwInfo& hw, int regs, dwb_plan* p) {
   p->tile_w_in = p->tile_w + K - 1;
   p->consumer_warps = cw;
   p->threads = 32 * (cw + 1);
-  p->reserved0 = 0;
   const long long smem = plan_smem_bytes(K, p->tile_w_in, p->ring_rows, S, slots, M, R, nullptr);
   if (smem > hw.smem_optin) return DWB_ERR_BAD_ARG;
   if (regs > 0 && ctas_by_registers(regs, cw + 1, hw.regs_per_sm) < 1) return DWB_ERR_BAD_ARG;

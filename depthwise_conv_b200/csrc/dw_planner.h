@@ -22,7 +22,7 @@ struct HwInfo {
 };
 
 // Register count of a compiled variant, or 0 when the variant is not built.
-typedef int (*RegsFn)(int K, int R, int M, int acc, void* ctx);
+typedef int (*RegsFn)(int K, int R, int M, int acc, int pre, void* ctx);
 
 // Register estimate used when no device is present (matches ptxas within a
 // few registers for the variants in dw_variants.cuh).
@@ -32,7 +32,10 @@ int estimate_regs(int K, int R, int M, int acc);
 constexpr int kNumVariantR = 6;
 extern const int kVariantR[kNumVariantR];
 extern const int kVariantM[2];
-bool variant_compiled(int K, int R, int M, int acc);
+bool variant_compiled(int K, int R, int M, int acc, int pre);
+
+// Load schedule the cost model assumes for a variant (the tuner measures both).
+int default_load_schedule(int K, int R, int M, int acc);
 
 // Dynamic shared memory of a plan: mbarriers, the stage ring (each stage =
 // one staged input row of tile_w_in pixels + one weight row of K taps), then

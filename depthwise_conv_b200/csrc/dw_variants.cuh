@@ -1,20 +1,23 @@
-// dw_variants.cuh -- the (R, M, ACC) variants compiled for every kernel size.
+// dw_variants.cuh -- the (R, M, ACC, PRE) variants compiled for every kernel size.
 //   R (columns per thread) in {7, 8, 14, 16} covers the widths 7, 14, 16, 28,
 //   32 and 56 without overhang, plus R in {28, 32} for K <= 13, where a wider
 //   register block amortises the per-kernel-row overhead over more FMAs;
 //   M (rows per thread) in {1, 2}; ACC 0 = fp32 FFMA2, 1 = fp16x2 chains with
-//   fp32 accumulation.  dw_planner.cpp (variant_compiled) mirrors this list.
+//   fp32 accumulation; PRE (load schedule, mixed mode only) 0 or 1.
+//   dw_planner.cpp (variant_compiled) mirrors this list.
 #pragma once
 #include "dw_kernel.cuh"
 
-#define DWB_ENTRY(K, R, M, A) {K, R, M, A, reinterpret_cast<const void*>(&::dwb::dw_stream_kernel<K, R, M, A>)}
-#define DWB_VARIANTS_ACC(K, A)                                                                      \
-  DWB_ENTRY(K, 7, 1, A), DWB_ENTRY(K, 7, 2, A), DWB_ENTRY(K, 8, 1, A), DWB_ENTRY(K, 8, 2, A),     \
-      DWB_ENTRY(K, 14, 1, A), DWB_ENTRY(K, 14, 2, A), DWB_ENTRY(K, 16, 1, A), DWB_ENTRY(K, 16, 2, A)
-#define DWB_WIDE_ACC(K, A) \
-  DWB_ENTRY(K, 28, 1, A), DWB_ENTRY(K, 28, 2, A), DWB_ENTRY(K, 32, 1, A), DWB_ENTRY(K, 32, 2, A)
-#define DWB_VARIANTS(K) DWB_VARIANTS_ACC(K, 0), DWB_VARIANTS_ACC(K, 1)
-#define DWB_VARIANTS_WIDE(K) DWB_VARIANTS(K), DWB_WIDE_ACC(K, 0), DWB_WIDE_ACC(K, 1)
+#define DWB_ENTRY(K, R, M, A, P) \
+  {K, R, M, A, P, reinterpret_cast<const void*>(&::dwb::dw_stream_kernel<K, R, M, A, P>)}
+#define DWB_VARIANTS_AP(K, A, P)                                                                            \
+  DWB_ENTRY(K, 7, 1, A, P), DWB_ENTRY(K, 7, 2, A, P), DWB_ENTRY(K, 8, 1, A, P), DWB_ENTRY(K, 8, 2, A, P),   \
+      DWB_ENTRY(K, 14, 1, A, P), DWB_ENTRY(K, 14, 2, A, P), DWB_ENTRY(K, 16, 1, A, P), DWB_ENTRY(K, 16, 2, A, P)
+#define DWB_WIDE_AP(K, A, P) \
+  DWB_ENTRY(K, 28, 1, A, P), DWB_ENTRY(K, 28, 2, A, P), DWB_ENTRY(K, 32, 1, A, P), DWB_ENTRY(K, 32, 2, A, P)
+#define DWB_VARIANTS(K) DWB_VARIANTS_AP(K, 0, 0), DWB_VARIANTS_AP(K, 1, 0), DWB_VARIANTS_AP(K, 1, 1)
+#define DWB_VARIANTS_WIDE(K) \
+  DWB_VARIANTS(K), DWB_WIDE_AP(K, 0, 0), DWB_WIDE_AP(K, 1, 0), DWB_WIDE_AP(K, 1, 1)
 
 #define DWB_DEFINE_TABLE_OF(K, LIST)                                                      \
   namespace dwb {                                                                         \

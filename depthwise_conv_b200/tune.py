@@ -26,7 +26,8 @@ DEFAULT_PROBLEMS = [
     (8, 56, 56, 1024, 7), (8, 56, 56, 1024, 31), (32, 56, 56, 1024, 9),
 ] + [(64, 56, 56, 1024, k) for k in (7, 9, 13, 17, 21, 27, 29, 31)]
 
-FIELDS = ("cols_per_thread", "rows_per_thread", "tile_h", "tile_w", "ring_rows", "ring_wrows", "grid", "row_splits")
+FIELDS = ("cols_per_thread", "rows_per_thread", "tile_h", "tile_w", "ring_rows", "ring_wrows", "grid", "row_splits",
+          "load_schedule")
 
 
 def time_plan(d, x, w, y, plan, accum, reps):
@@ -66,8 +67,11 @@ def tune_problem(B, H, W, C, K, accum, budget):
     best = (default, None)
     t0 = time.time()
     for c in cands:
-        for grid in (-1, 0):  # persistent, or one tile per CTA
-            plan = dict(c, grid=grid)
+        for grid, pre in ((-1, c["load_schedule"]), (0, c["load_schedule"]), (-1, 1 - c["load_schedule"]),
+                          (0, 1 - c["load_schedule"])):  # persistent or one tile per CTA; both load schedules
+            if pre == 1 and accum != _lib.ACCUM_MIXED:
+                continue
+            plan = dict(c, grid=grid, load_schedule=pre)
             try:
                 us = time_plan(d, x, w, y, plan, accum, reps)
             except RuntimeError:
@@ -82,7 +86,7 @@ def tune_problem(B, H, W, C, K, accum, budget):
 def write_table(rows, path):
     lines = ["// dw_tuned_plans.inc -- plans measured fastest on B200 by depthwise_conv_b200/tune.py.",
              "// {B, H, W, C, K, accum, R, M, tile_h, tile_w, ring_rows, ring_wrows, grid(-1 persistent, 0 one tile/CTA),",
-             "//  row_splits}"]
+             "//  row_splits, load_schedule}"]
     old = []
     if os.path.exists(TABLE):  # start from the committed table
         for ln in open(TABLE):

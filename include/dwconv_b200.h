@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define DWB_ABI_VERSION 3
+#define DWB_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define DWB_API __attribute__((visibility("default")))
@@ -97,7 +97,9 @@ typedef struct dwb_plan {
     int32_t row_splits;         /* S: warps sharing one output slot, each taking
                                    every S-th kernel row; their fp32 partial sums
                                    are added in shared memory (0 or 1 = none)    */
-    int32_t reserved0;          /* zero                                          */
+    int32_t load_schedule;      /* 0: input columns read next to their FMAs;
+                                   1: the row segment read into registers first
+                                   (mixed accumulation only)                     */
 } dwb_plan;
 
 /* ---- library information ------------------------------------------------ */

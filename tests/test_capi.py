@@ -39,7 +39,7 @@ def test_every_declared_symbol_is_exported_and_bound(lib):
 
 def test_abi_version_and_status_strings(lib):
     from depthwise_conv_b200 import _lib
-    assert lib.dwb_abi_version() == 3
+    assert lib.dwb_abi_version() == 4
     for code in range(9):
         assert lib.dwb_status_string(code) and b"unknown" not in lib.dwb_status_string(code)
     assert lib.dwb_status_string(99) == b"unknown status"
@@ -101,6 +101,7 @@ def test_plans_respect_hardware_limits(B, H, W, C, K, accum):
     assert (R in (7, 8, 14, 16) or (R in (28, 32) and K <= 13)) and M in (1, 2)
     assert p["tile_w"] % R == 0 and p["tile_h"] % M == 0
     assert p["tile_w_in"] == p["tile_w"] + K - 1 <= 256                 # TMA box limit
+    assert p["load_schedule"] in ((0, 1) if accum == 1 else (0,))
     S = p["row_splits"]
     assert 1 <= S <= K
     assert p["consumer_warps"] == S * (p["tile_w"] // R) * (p["tile_h"] // M)

@@ -179,6 +179,35 @@ def test_row_split_plans(eng, oracle_mod, B, H, W, C, K, accum):
     assert eng.device_error() == 0
 
 
+@pytest.mark.parametrize("B,H,W,C,K", [(2, 19, 33, 128, 7), (1, 21, 30, 64, 17), (2, 9, 12, 136, 31), (1, 32, 32, 192, 9)])
+def test_both_load_schedules(eng, oracle_mod, B, H, W, C, K):
+    """Mixed-mode variants come in two load schedules (row read up front, or per column); both agree
+    with the oracle for every register-block shape the planner offers."""
+    from depthwise_conv_b200 import _lib
+    x, w = make_problem(300 + K, B, H, W, C, K)
+    exact, _ = oracle_mod.dw_forward(x, w)
+    xd, wd = to_dev(x), to_dev(w)
+    seen = set()
+    for c in sorted(_lib.plan_candidates(B, H, W, C, K, 1), key=lambda c: c["model_cost"]):
+        key = (c["cols_per_thread"], c["rows_per_thread"])
+        if key in seen:
+            continue
+        seen.add(key)
+        outs = []
+        for pre in (0, 1):
+            try:
+                y = eng.conv2d_nhwc_fused(xd, wd, accum=1, plan=dict(c, load_schedule=pre, grid=-1))
+            except _lib.DwbError as e:  # host-side candidate whose real register count does not fit
+                assert e.status == _lib.ERR_BAD_ARG
+                continue
+            torch.cuda.synchronize()
+            assert_parity(oracle_mod, y, exact, tight=False, what=f"R={key[0]} M={key[1]} pre={pre}")
+            outs.append(y)
+        if len(outs) == 2:
+            assert torch.equal(outs[0], outs[1])  # same arithmetic, only the load order differs
+    assert len(seen) >= 4
+
+
 @pytest.mark.parametrize("act", ["none", "relu", "gelu"])
 @pytest.mark.parametrize("terms", ["bias", "bias_bn", "bias_bn_res", "bn_res"])
 def test_fused_epilogue(eng, oracle_mod, act, terms):
