@@ -7,11 +7,22 @@ into the package directory.  Objects are rebuilt only when a source or any
 header is newer.  The library depends on the CUDA runtime only (no torch).
 
     python -m depthwise_conv_b200.csrc.build        # or: python build.py
+    python -m depthwise_conv_b200.csrc.build --regcaps   # regenerate dw_regcaps.inc first
+
+Register caps.  How many warps an SM holds is set by the registers per
+thread in steps (64, 72, 80, 96, 128, 168, 255 registers = 8 ... 2 warps per
+sub-partition), and ptxas often lands a few registers above a step.
+``--regcaps`` compiles every kernel variant uncapped, reads the register
+counts ptxas reports, caps each variant that is at most 10 registers above a
+step at that step (``__maxnreg__``), recompiles, and uncaps any capped variant
+that then spills more than 32 bytes.  The result is ``dw_regcaps.inc``, committed with the
+sources; a plain build uses it.
 """
 from __future__ import annotations
 
 import concurrent.futures as cf
 import os
+import re
 import shutil
 import subprocess
 import sys
@@ -82,6 +93,76 @@ def build(verbose: bool = False, jobs: int | None = None) -> str:
     return LIB
 
 
+REGCAPS = os.path.join(HERE, "dw_regcaps.inc")
+_STEPS = (64, 72, 80, 96, 128, 168, 255)
+_SPILL_OK = 32  # bytes of spill stores a cap may cost (a few loop-invariant words)
+_ENTRY = re.compile(r"Compiling entry function '\S*dw_stream_kernel(?:_capped)?ILi(\d+)ELi(\d+)ELi(\d+)ELi(\d+)ELi(\d+)E")
+_USED = re.compile(r"Used (\d+) registers")
+_SPILL = re.compile(r"(\d+) bytes spill stores")
+
+
+def _ptxas_report(src: str, extra: list[str]) -> dict:
+    """{(K, R, M, acc, pre): (registers, spill bytes)} of the kernel variants in one source file."""
+    cmd = [_nvcc(), *ARCH, *NVCC_FLAGS, *extra, "-Xptxas", "-v", "-I", INCLUDE, "-c", src, "-o", os.devnull]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"compile failed: {' '.join(cmd)}\n{res.stdout}\n{res.stderr}")
+    out, key, spill = {}, None, 0
+    for line in res.stderr.splitlines():
+        m = _ENTRY.search(line)
+        if m:
+            key, spill = tuple(int(v) for v in m.groups()), 0
+            continue
+        m = _SPILL.search(line)
+        if m and key:
+            spill = int(m.group(1))
+        m = _USED.search(line)
+        if m and key:
+            out[key] = (int(m.group(1)), spill)
+            key = None
+    return out
+
+
+def _reports(extra: list[str]) -> dict:
+    srcs = sorted(os.path.join(HERE, f) for f in os.listdir(HERE) if f.startswith("dw_kernels_k") and f.endswith(".cu"))
+    merged = {}
+    with cf.ThreadPoolExecutor(max_workers=max(1, os.cpu_count() or 4)) as ex:
+        for rep in ex.map(lambda f: _ptxas_report(f, extra), srcs):
+            merged.update(rep)
+    return merged
+
+
+def _write_caps(caps: dict) -> None:
+    lines = ["// dw_regcaps.inc -- per-variant register caps, generated by build.py --regcaps.",
+             "// {K, R, M, ACC, PRE, max registers}"]
+    lines += ["{%d, %d, %d, %d, %d, %d}," % (*k, c) for k, c in sorted(caps.items()) if c < 255]
+    with open(REGCAPS, "w") as f:
+        f.write("\n".join(lines) + "\n")
+
+
+def regcaps(verbose: bool = False) -> dict:
+    """Regenerate dw_regcaps.inc from ptxas's register counts (see the module docstring)."""
+    natural = _reports(["-DDWB_NO_REGCAPS"])
+    caps = {}
+    for key, (regs, _) in natural.items():
+        step = max(b for b in _STEPS if b <= regs) if regs >= _STEPS[0] else regs
+        caps[key] = step if (regs > step and regs - step <= 10) else 255
+    _write_caps(caps)
+    capped = _reports([])
+    for key, (regs, spill) in capped.items():
+        if caps.get(key, 255) < 255 and spill > _SPILL_OK:
+            caps[key] = 255  # the cap made ptxas spill more than a few words: leave this variant alone
+    _write_caps(caps)
+    if verbose:
+        for key in sorted(caps):
+            if caps[key] < 255:
+                print(f"K={key[0]} R={key[1]} M={key[2]} acc={key[3]} pre={key[4]}: "
+                      f"{natural[key][0]} -> {capped[key][0]} registers")
+    return caps
+
+
 if __name__ == "__main__":
+    if "--regcaps" in sys.argv:
+        regcaps(verbose=True)
     print(build(verbose=True))
     sys.exit(0)

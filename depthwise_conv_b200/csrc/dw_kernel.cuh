@@ -47,10 +47,9 @@
 //
 // Row split (S > 1, for small images where tiles are few)
 //   S warps share each output slot; warp group g computes the kernel rows
-//   s_lo + g, s_lo + g + S, ... into fp32 accumulators (group 0 starts from
-//   the bias, the others from zero).  At the end of the tile groups 1..S-1
-//   store their accumulators in a shared-memory exchange area and group 0
-//   adds them before the epilogue.  The hand-off is two mbarriers (partials
+//   s_lo + g, s_lo + g + S, ... into fp32 accumulators.  At the end of the
+//   tile groups 1..S-1 store their accumulators in a shared-memory exchange
+//   area and group 0 adds them before the epilogue.  The hand-off is two mbarriers (partials
 //   written / area free again) with bounded waits, so a failing warp can
 //   never leave the others blocked.  Every warp still waits for and releases
 //   every stage in order, which keeps the ring protocol unchanged.
@@ -161,11 +160,7 @@ __device__ __forceinline__ void step_rows(f32x2 (&acc)[M][R], const __half2* __r
     for (int m = 0; m < M; ++m) {
       if (m == 0 ? v0 : v1) {
         const __half2* xrow = m == 0 ? xrow0 : xrow1;
-        __half2 part[SPLIT][R];
-#pragma unroll
-        for (int c = 0; c < SPLIT; ++c)
-#pragma unroll
-          for (int r = 0; r < R; ++r) part[c][r] = __float2half2_rn(0.f);
+        __half2 part[SPLIT][R];  // each chain starts with a product (no zero initialisation)
         __half2 xs[PRE ? NJ : 1];
         if constexpr (PRE) {
 #pragma unroll
@@ -184,7 +179,8 @@ __device__ __forceinline__ void step_rows(f32x2 (&acc)[M][R], const __half2* __r
             const int kj = j - r;
             if (kj >= 0 && kj < K) {
               const int c = (SPLIT == 2 && kj >= K / 2 + 1) ? 1 : 0;
-              part[c][r] = __hfma2(xv, wv[kj], part[c][r]);
+              const bool first = kj == 0 || (SPLIT == 2 && kj == K / 2 + 1);
+              part[c][r] = first ? __hmul2(xv, wv[kj]) : __hfma2(xv, wv[kj], part[c][r]);
             }
           }
         }
@@ -197,14 +193,13 @@ __device__ __forceinline__ void step_rows(f32x2 (&acc)[M][R], const __half2* __r
   }
 }
 
-// Epilogue of one warp slot: y = act(acc) * scale + shift (+ residual), where
-// the accumulators already started from the bias.  ACT / RES / FULL are
+// Epilogue of one warp slot: y = act(acc + bias) * scale + shift (+ residual).  ACT / RES / FULL are
 // resolved once per tile by the caller, so the loop is straight-line code
 // (FULL: every row and column of the slot is inside the image).
 template <int ACT, bool RES, bool FULL, int M, int R>
-__device__ __forceinline__ void store_slot(const f32x2 (&acc)[M][R], f32x2 scale, f32x2 shift, __half2* y,
-                                           const __half2* res, long long row_h2, int col_h2, int rows_valid,
-                                           int cols_valid) {
+__device__ __forceinline__ void store_slot(const f32x2 (&acc)[M][R], f32x2 bias, f32x2 scale, f32x2 shift,
+                                           __half2* y, const __half2* res, long long row_h2, int col_h2,
+                                           int rows_valid, int cols_valid) {
 #pragma unroll
   for (int m = 0; m < M; ++m) {
     if (!FULL && m >= rows_valid) break;
@@ -214,6 +209,7 @@ __device__ __forceinline__ void store_slot(const f32x2 (&acc)[M][R], f32x2 scale
     for (int r = 0; r < R; ++r) {
       if (!FULL && r >= cols_valid) break;
       f32x2 a = acc[m][r];
+      fadd2(a, bias);
       if (ACT == kActGelu) {
         a = gelu_erf2(a);
       } else if (ACT == kActRelu) {
@@ -229,18 +225,35 @@ __device__ __forceinline__ void store_slot(const f32x2 (&acc)[M][R], f32x2 scale
 }
 
 template <int ACT, bool RES, int M, int R>
-__device__ __forceinline__ void store_tile_slot(const f32x2 (&acc)[M][R], f32x2 scale, f32x2 shift, __half2* y,
-                                                const __half2* res, long long row_h2, int col_h2, int rows_valid,
-                                                int cols_valid) {
+__device__ __forceinline__ void store_tile_slot(const f32x2 (&acc)[M][R], f32x2 bias, f32x2 scale, f32x2 shift,
+                                                __half2* y, const __half2* res, long long row_h2, int col_h2,
+                                                int rows_valid, int cols_valid) {
   if (rows_valid == M && cols_valid == R)
-    store_slot<ACT, RES, true>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid);
+    store_slot<ACT, RES, true>(acc, bias, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid);
   else
-    store_slot<ACT, RES, false>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid);
+    store_slot<ACT, RES, false>(acc, bias, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid);
+}
+
+// Register cap of a variant (dw_regcaps.inc; 255 = none).
+struct RegCap {
+  int k, r, m, acc, pre, cap;
+};
+constexpr RegCap kRegCaps[] = {
+#include "dw_regcaps.inc"
+    {0, 0, 0, 0, 0, 255}};
+template <int K, int R, int M, int ACC, int PRE>
+constexpr int reg_cap() {
+#ifdef DWB_NO_REGCAPS
+  return 255;
+#else
+  for (const RegCap& c : kRegCaps)
+    if (c.k == K && c.r == R && c.m == M && c.acc == ACC && c.pre == PRE) return c.cap;
+  return 255;
+#endif
 }
 
 template <int K, int R, int M, int ACC, int PRE>
-__global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
-                                 const __grid_constant__ CUtensorMap tmap_w, const DwParams p) {
+__device__ __forceinline__ void dw_stream_body(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const DwParams& p) {
   constexpr int PAD = K / 2;
   extern __shared__ __align__(1024) unsigned char smem[];
 
@@ -343,12 +356,13 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
       shift = f2_bits(sh);
     }
 
-    f32x2 acc[M][R];  // packed fp32 (channel 2l, channel 2l+1), starting from the bias
-    const f32x2 acc0 = sg == 0 ? bias : f32x2_zero();
+    // packed fp32 (channel 2l, channel 2l+1); the bias is added in the epilogue, so the
+    // parameter loads above are not waited for before the first step
+    f32x2 acc[M][R];
 #pragma unroll
     for (int m = 0; m < M; ++m)
 #pragma unroll
-      for (int r = 0; r < R; ++r) acc[m][r] = acc0;
+      for (int r = 0; r < R; ++r) acc[m][r] = f32x2_zero();
     int turn = sg;  // steps until this warp's next kernel row
 
     // warps whose columns all lie right of the image have nothing to compute
@@ -441,14 +455,38 @@ __global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
       const long long row_h2 = static_cast<long long>(p.W) * p.C / 2;
       const int col_h2 = p.C / 2;
       switch (p.act * 2 + (res != nullptr)) {  // one branch per tile, then straight-line stores
-        case 0: store_tile_slot<kActNone, false>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
-        case 1: store_tile_slot<kActNone, true>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
-        case 2: store_tile_slot<kActRelu, false>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
-        case 3: store_tile_slot<kActRelu, true>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
-        case 4: store_tile_slot<kActGelu, false>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
-        default: store_tile_slot<kActGelu, true>(acc, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
+        case 0: store_tile_slot<kActNone, false>(acc, bias, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
+        case 1: store_tile_slot<kActNone, true>(acc, bias, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
+        case 2: store_tile_slot<kActRelu, false>(acc, bias, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
+        case 3: store_tile_slot<kActRelu, true>(acc, bias, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
+        case 4: store_tile_slot<kActGelu, false>(acc, bias, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
+        default: store_tile_slot<kActGelu, true>(acc, bias, scale, shift, y, res, row_h2, col_h2, rows_valid, cols_valid); break;
       }
     }
+  }
+}
+
+// The kernel, without and with a register cap.  A variant without an entry
+// in dw_regcaps.inc is compiled with no __maxnreg__ at all (ptxas's own
+// choice), one with an entry under that cap.
+template <int K, int R, int M, int ACC, int PRE>
+__global__ void dw_stream_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                                 const __grid_constant__ CUtensorMap tmap_w, const DwParams p) {
+  dw_stream_body<K, R, M, ACC, PRE>(tmap_x, tmap_w, p);
+}
+template <int K, int R, int M, int ACC, int PRE, int CAP>
+__global__ void __maxnreg__(CAP) dw_stream_kernel_capped(const __grid_constant__ CUtensorMap tmap_x,
+                                                         const __grid_constant__ CUtensorMap tmap_w,
+                                                         const DwParams p) {
+  dw_stream_body<K, R, M, ACC, PRE>(tmap_x, tmap_w, p);
+}
+template <int K, int R, int M, int ACC, int PRE>
+inline const void* kernel_fn() {
+  constexpr int cap = reg_cap<K, R, M, ACC, PRE>();
+  if constexpr (cap < 255) {
+    return reinterpret_cast<const void*>(&dw_stream_kernel_capped<K, R, M, ACC, PRE, cap>);
+  } else {
+    return reinterpret_cast<const void*>(&dw_stream_kernel<K, R, M, ACC, PRE>);
   }
 }
 

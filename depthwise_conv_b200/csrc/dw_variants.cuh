@@ -8,8 +8,7 @@
 #pragma once
 #include "dw_kernel.cuh"
 
-#define DWB_ENTRY(K, R, M, A, P) \
-  {K, R, M, A, P, reinterpret_cast<const void*>(&::dwb::dw_stream_kernel<K, R, M, A, P>)}
+#define DWB_ENTRY(K, R, M, A, P) {K, R, M, A, P, ::dwb::kernel_fn<K, R, M, A, P>()}
 #define DWB_VARIANTS_AP(K, A, P)                                                                            \
   DWB_ENTRY(K, 7, 1, A, P), DWB_ENTRY(K, 7, 2, A, P), DWB_ENTRY(K, 8, 1, A, P), DWB_ENTRY(K, 8, 2, A, P),   \
       DWB_ENTRY(K, 14, 1, A, P), DWB_ENTRY(K, 14, 2, A, P), DWB_ENTRY(K, 16, 1, A, P), DWB_ENTRY(K, 16, 2, A, P)
