@@ -4,9 +4,11 @@
 
 For every problem (default: the benchmark configurations) the candidates
 from ``dwb_plan_candidates`` are timed in the planner's cost order (CUDA
-graph of back-to-back launches, best of 3) until the per-problem time budget
-runs out; the fastest plan is written to ``csrc/dw_tuned_plans.inc``, which
-the library consults before its cost model (rebuild afterwards).  Results
+graph of back-to-back launches, best of 3) on a proxy batch of at most
+``--proxy-batch`` images until the per-problem time budget runs out; the
+fastest few are then timed on the full batch (both load schedules, both grid
+modes) and the winner is written to ``csrc/dw_tuned_plans.inc``, which the
+library consults before its cost model (rebuild afterwards).  Results
 are also printed as JSON lines.
 """
 from __future__ import annotations
@@ -53,33 +55,61 @@ def time_plan(d, x, w, y, plan, accum, reps):
     return best
 
 
-def tune_problem(B, H, W, C, K, accum, budget):
+def _inputs(B, H, W, C, K):
     import torch
+    x = torch.randn(B, C, H, W, device="cuda").half().contiguous(memory_format=torch.channels_last)
+    w = (torch.randn(K, K, C, device="cuda") / K).half()
+    return x, w, torch.empty_like(x)
+
+
+def _reps(B, H, W, C):
+    return 3 if B * H * W * C >= (64 << 20) else (10 if B >= 16 else 50)
+
+
+def tune_problem(B, H, W, C, K, accum, budget, proxy_batch=8, finalists=8):
+    """Phase 1 ranks the candidates (model order, both grid modes, the model's load schedule) on
+    min(B, proxy_batch) images until the budget is spent; phase 2 times the best `finalists`
+    on the full batch with both load schedules and both grid modes."""
     import depthwise_conv_b200 as d
     from depthwise_conv_b200 import _lib
 
-    x = torch.randn(B, C, H, W, device="cuda").half().contiguous(memory_format=torch.channels_last)
-    w = (torch.randn(K, K, C, device="cuda") / K).half()
-    y = torch.empty_like(x)
     cands = sorted(_lib.plan_candidates(B, H, W, C, K, accum), key=lambda c: c["model_cost"])
-    reps = 3 if B * H * W * C >= (64 << 20) else (10 if B >= 16 else 50)
-    default = time_plan(d, x, w, y, None, accum, reps)
-    best = (default, None)
+    Bp = min(B, proxy_batch)
+    xp, wp, yp = _inputs(Bp, H, W, C, K)
+    ranked = []
     t0 = time.time()
     for c in cands:
-        for grid, pre in ((-1, c["load_schedule"]), (0, c["load_schedule"]), (-1, 1 - c["load_schedule"]),
-                          (0, 1 - c["load_schedule"])):  # persistent or one tile per CTA; both load schedules
+        for grid in (-1, 0):
+            plan = dict(c, grid=grid)
+            try:
+                ranked.append((time_plan(d, xp, wp, yp, plan, accum, _reps(Bp, H, W, C)), plan))
+            except RuntimeError:
+                continue
+        if time.time() - t0 > budget:
+            break
+    del xp, wp, yp
+    x, w, y = _inputs(B, H, W, C, K)
+    reps = _reps(B, H, W, C)
+    default = time_plan(d, x, w, y, None, accum, reps)
+    best = (default, None)
+    seen = set()
+    for _, plan in sorted(ranked, key=lambda r: r[0]):
+        key = tuple(sorted((k, v) for k, v in plan.items() if k in FIELDS))
+        if key in seen:
+            continue
+        seen.add(key)
+        if len(seen) > finalists:
+            break
+        for pre in (plan["load_schedule"], 1 - plan["load_schedule"]):
             if pre == 1 and accum != _lib.ACCUM_MIXED:
                 continue
-            plan = dict(c, grid=grid, load_schedule=pre)
+            cand = dict(plan, load_schedule=pre)
             try:
-                us = time_plan(d, x, w, y, plan, accum, reps)
+                us = time_plan(d, x, w, y, cand, accum, reps)
             except RuntimeError:
                 continue
             if us < best[0]:
-                best = (us, plan)
-        if time.time() - t0 > budget:
-            break
+                best = (us, cand)
     return default, best
 
 
@@ -110,6 +140,8 @@ def main():
     ap.add_argument("problems", nargs="*", help="B,H,W,C,K (default: the benchmark configurations)")
     ap.add_argument("--budget", type=float, default=20.0, help="seconds of candidate timing per problem")
     ap.add_argument("--accum", choices=["mixed", "f32"], default="mixed")
+    ap.add_argument("--proxy-batch", type=int, default=8, help="images per timing while ranking candidates")
+    ap.add_argument("--finalists", type=int, default=8, help="plans re-timed on the full batch")
     ap.add_argument("--no-write", action="store_true")
     ap.add_argument("--out", default=TABLE, help="where to write the merged table (default: the library's)")
     args = ap.parse_args()
@@ -118,7 +150,7 @@ def main():
     probs = [tuple(int(v) for v in p.split(",")) for p in args.problems] or DEFAULT_PROBLEMS
     rows = []
     for B, H, W, C, K in probs:
-        default, (us, plan) = tune_problem(B, H, W, C, K, accum, args.budget)
+        default, (us, plan) = tune_problem(B, H, W, C, K, accum, args.budget, args.proxy_batch, args.finalists)
         print(json.dumps({"problem": [B, H, W, C, K], "accum": args.accum, "default_us": default, "best_us": us,
                           "plan": {f: plan[f] for f in FIELDS} if plan else None}), flush=True)
         if plan is not None:
