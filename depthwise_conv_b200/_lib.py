@@ -82,6 +82,7 @@ SIGNATURES = {
     "dwb_bias_act_affine_nhwc": ([_p, _p, _p, _p, _p, _i64, _i64, _i, _p], _i),
     "dwb_device_error": ([ctypes.POINTER(ctypes.c_int), _i, _p], _i),
     "dwb_probe_fma_peak": ([ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double), _p], _i),
+    "dwb_selftest_bounded_wait": ([_i64, _p], _i),
 }
 
 _lib = None
@@ -176,6 +177,12 @@ def device_error(stream: int = 0, clear: bool = True) -> int:
     code = ctypes.c_int(0)
     check("dwb_device_error", load().dwb_device_error(ctypes.byref(code), int(clear), stream))
     return code.value
+
+
+def selftest_bounded_wait(limit_cycles: int = 2_000_000, stream: int = 0) -> int:
+    """Run the bounded-wait self-test kernel and return the device error code it left (5 expected)."""
+    check("dwb_selftest_bounded_wait", load().dwb_selftest_bounded_wait(int(limit_cycles), stream))
+    return device_error(stream)
 
 
 def probe_fma_peak(stream: int = 0) -> tuple[float, float]:

@@ -65,6 +65,20 @@ static const KernelEntry* find_variant(int K, int R, int M, int acc, int pre) {
   return nullptr;
 }
 
+// Self-test of the bounded-wait path: one thread waits on an mbarrier that
+// nothing ever arrives at.  The wait gives up after `limit` cycles, records
+// code 5 in the device error word and the kernel returns normally, so the
+// context stays usable -- the same path a kernel takes when its data never
+// arrives.
+__global__ void bounded_wait_selftest(int* err, long long limit) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    (void)mbar_wait_bounded(&bar, 0u, err, 5, limit);
+  }
+}
+
 // ---- per-device state -----------------------------------------------------------
 // The device error word: written by kernels whose bounded waits expire.
 static __device__ int g_device_error;
@@ -591,6 +605,16 @@ int dwb_depthwise_29x29_256_nhwc(const void* input, const void* weight, const vo
 int dwb_depthwise_27x27_512_nhwc(const void* input, const void* weight, const void* bias, void* output, int B, int C,
                                  int H, int W, void* stream) {
   return replknet_forward(input, weight, bias, output, B, C, H, W, 512, 14, 27, stream);
+}
+
+int dwb_selftest_bounded_wait(int64_t limit_cycles, void* stream) {
+  if (limit_cycles < 1 || limit_cycles > kWaitLimitCycles) return DWB_ERR_BAD_ARG;
+  DeviceState* st = nullptr;
+  int rc = get_device_state(&st);
+  if (rc != DWB_OK) return rc;
+  bounded_wait_selftest<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(st->err_word, limit_cycles);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? DWB_OK : cuda_fail("launch(bounded_wait_selftest)", e);
 }
 
 int dwb_device_error(int* code_out, int clear, void* stream) {

@@ -13,7 +13,8 @@ namespace dwb {
 // Error codes a kernel stores in the device error word (first writer wins)
 // when one of its bounded waits expires: 1 = stage wait before a tile's
 // first step, 2 = stage wait of a step, 3 = producer's free-stage (empty)
-// wait, 4 = row-split partial-sum hand-off.  The word lives in the launcher's
+// wait, 4 = row-split partial-sum hand-off, 5 = the bounded-wait self-test
+// (dwb_selftest_bounded_wait), whose wait nothing ever completes.  The word lives in the launcher's
 // translation unit; kernels receive its address.
 
 // ~1 s at 2 GHz: far above any legitimate wait (a row load takes ~1 us).
@@ -69,13 +70,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity to complete.  Returns false (and
-// records `code` in *err) if it has not completed within kWaitLimitCycles.
+// records `code` in *err) if it has not completed within `limit` clock cycles
+// (kWaitLimitCycles unless a self-test asks for less).
 template <bool SLEEP = false>
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err, int code) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err, int code,
+                                                  long long limit = kWaitLimitCycles) {
   if (mbar_try_wait<SLEEP>(bar, parity)) return true;
   const long long t0 = clock64();
   while (!mbar_try_wait<SLEEP>(bar, parity)) {
-    if (clock64() - t0 > kWaitLimitCycles) {
+    if (clock64() - t0 > limit) {
       atomicCAS(err, 0, code);
       return false;
     }

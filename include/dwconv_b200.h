@@ -220,6 +220,14 @@ DWB_API int dwb_depthwise_27x27_512_nhwc(const void* input, const void* weight, 
  * mbarrier wait expired.  Synchronises the given stream first. */
 DWB_API int dwb_device_error(int* code_out, int clear, void* stream);
 
+/* Self-test of the failure path: launch a one-warp kernel whose bounded
+ * mbarrier wait can never complete, with a limit of limit_cycles clock
+ * cycles (1 .. 2e9).  The wait expires, the kernel records code 5 in the
+ * device error word (read it with dwb_device_error) and returns; the context
+ * stays usable.  No counterpart in the reference, whose kernels have no
+ * waits. */
+DWB_API int dwb_selftest_bounded_wait(int64_t limit_cycles, void* stream);
+
 /* Measure the CUDA-core FMA rate of the current device with a short
  * microbenchmark (fp16x2 HFMA2 and fp32x2 FFMA2), in TFLOP/s. */
 DWB_API int dwb_probe_fma_peak(double* hfma2_tflops, double* ffma2_tflops, void* stream);

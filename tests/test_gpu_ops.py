@@ -262,3 +262,21 @@ def test_probe_fma_peak_reports_plausible_rates(eng):
 
 def test_device_error_word_clear(eng):
     assert eng.device_error() == 0
+
+
+def test_expired_wait_reports_and_context_survives(eng, oracle_mod):
+    """Failure path on the GPU without a fault: a kernel whose mbarrier wait nothing completes gives up
+    after ~1 ms, leaves code 5 in the device error word and returns; the next convolution still runs
+    and matches the oracle, and the word reads clean again."""
+    from depthwise_conv_b200 import _lib
+    assert eng.device_error() == 0
+    assert _lib.selftest_bounded_wait(2_000_000) == 5
+    assert eng.device_error() == 0  # cleared by the read
+    x, w = make_problem(5, 1, 16, 16, 64, 7)
+    y = eng.conv2d_nhwc_fused(to_dev(x), to_dev(w))
+    torch.cuda.synchronize()
+    exact, _ = oracle_mod.dw_forward(x, w)
+    check(oracle_mod, y, exact, "after the self-test")
+    assert eng.device_error() == 0
+    with pytest.raises(_lib.DwbError):
+        _lib.selftest_bounded_wait(0)
