@@ -139,3 +139,21 @@ def test_plan_rejects_bad_problems():
         _lib.plan_query(1, 8, 8, 64, 6)
     with pytest.raises(_lib.DwbError):
         _lib.plan_query(1, 8, 8, 12, 7)
+
+
+def test_register_cap_table_is_consistent():
+    """dw_regcaps.inc (generated by build.py --regcaps) names only compiled variants, and every cap is one
+    of the occupancy steps the generator uses."""
+    import os
+    import re
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "depthwise_conv_b200", "csrc",
+                        "dw_regcaps.inc")
+    rows = [tuple(int(v) for v in m.groups())
+            for m in re.finditer(r"\{(\d+), (\d+), (\d+), (\d+), (\d+), (\d+)\}", open(path).read())]
+    assert rows, "empty register-cap table"
+    assert len(set(r[:5] for r in rows)) == len(rows)  # one cap per variant
+    for K, R, M, acc, pre, cap in rows:
+        assert K % 2 == 1 and 1 <= K <= 31 and M in (1, 2) and acc in (0, 1) and pre in (0, 1)
+        assert R in (7, 8, 14, 16) or (R in (28, 32) and K <= 13)
+        assert pre == 0 or acc == 1  # the read-ahead schedule exists in mixed mode only
+        assert cap in (64, 72, 80, 96, 128, 168)
