@@ -111,6 +111,14 @@ class FusedDWBlock(nn.Module):
                                                      self.act_code)
 
 
+def _epilogue(z, bias, scale, shift, act):
+    """act(z + bias) * scale + shift: in place in eager mode; under torch.compile through the
+    registered op ``depthwise::bias_act_affine`` (out of place, so the graph stays functional)."""
+    if torch.compiler.is_compiling():
+        return torch.ops.depthwise.bias_act_affine(z, bias, scale, shift, dw_ops.ACT_CODES[act])
+    return dw_ops.bias_act_affine(z, bias, scale, shift, act, out=z)
+
+
 class FusedPointwiseBlock(nn.Module):
     """1x1 conv -> act -> BN as a cuBLAS GEMM on the NHWC pixels plus one elementwise pass.
 
@@ -137,7 +145,7 @@ class FusedPointwiseBlock(nn.Module):
         B, C, H, W = x.shape
         z = torch.mm(x.permute(0, 2, 3, 1).reshape(B * H * W, C), self.weight_t)  # [BHW, C_out], NHWC
         z = z.view(B, H, W, -1).permute(0, 3, 1, 2)  # channels_last view
-        return dw_ops.bias_act_affine(z, self.bias, self.scale, self.shift, self.act, out=z)
+        return _epilogue(z, self.bias, self.scale, self.shift, self.act)
 
 
 class FusedStem(nn.Module):
@@ -161,7 +169,7 @@ class FusedStem(nn.Module):
         z = torch.nn.functional.conv2d(x, self.weight, None, self.stride)
         if not z.is_contiguous(memory_format=torch.channels_last):
             z = z.contiguous(memory_format=torch.channels_last)
-        return dw_ops.bias_act_affine(z, self.bias, self.scale, self.shift, self.act, out=z)
+        return _epilogue(z, self.bias, self.scale, self.shift, self.act)
 
 
 def fuse_dw_blocks(model: ConvMixer, pointwise: bool = True) -> ConvMixer:

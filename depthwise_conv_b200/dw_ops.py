@@ -150,6 +150,10 @@ torch.library.define(
     "depthwise::conv2d_nhwc_fused",
     "(Tensor input, Tensor weight, Tensor? bias, Tensor? scale, Tensor? shift, Tensor? residual, int act) -> Tensor",
 )
+torch.library.define(
+    "depthwise::bias_act_affine",
+    "(Tensor input, Tensor? bias, Tensor? scale, Tensor? shift, int act) -> Tensor",
+)
 
 
 @torch.library.impl("depthwise::conv2d_nhwc", "default")
@@ -169,4 +173,14 @@ def _conv2d_nhwc_fake(input, weight, bias=None):
 
 @torch.library.register_fake("depthwise::conv2d_nhwc_fused")
 def _conv2d_nhwc_fused_fake(input, weight, bias, scale, shift, residual, act):
+    return torch.empty_like(input)
+
+
+@torch.library.impl("depthwise::bias_act_affine", "default")
+def _bias_act_affine_impl(input, bias, scale, shift, act):
+    return bias_act_affine(input, bias, scale, shift, act)
+
+
+@torch.library.register_fake("depthwise::bias_act_affine")
+def _bias_act_affine_fake(input, bias, scale, shift, act):
     return torch.empty_like(input)

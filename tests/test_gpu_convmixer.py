@@ -86,3 +86,27 @@ def test_convmixer_cuda_graph_replay_tracks_inputs():
         assert (o - r).abs().max().item() == 0.0
     diffs = [(outs[i] - outs[i + 1]).abs().max().item() for i in range(3)]
     assert all(d > 0 for d in diffs)
+
+
+def test_convmixer_compiled_reduce_overhead_replay():
+    """The fused network under torch.compile(mode="reduce-overhead", fullgraph=True): the engine's
+    ops trace through their fake impls without graph breaks, the compiled forward matches eager, and
+    replays of the captured graph follow changing inputs (verify_e5b_correctness.py:26-37)."""
+    from depthwise_conv_b200.convmixer import convmixer, fuse_dw_blocks
+
+    full = fuse_dw_blocks(convmixer("1536_20", seed=0).half().cuda().to(memory_format=torch.channels_last))
+    model = full.model[:6]  # stem + 3 blocks (see test_convmixer_cuda_graph_replay_tracks_inputs)
+    compiled = torch.compile(model, mode="reduce-overhead", fullgraph=True)
+    mk = lambda: torch.randn(1, 3, 224, 224, device="cuda").half().contiguous(memory_format=torch.channels_last)  # noqa: E731
+    outs = []
+    with torch.no_grad():
+        for i in range(5):
+            xi = mk()
+            yc = compiled(xi).clone()
+            ye = model(xi)
+            torch.cuda.synchronize()
+            err = ((yc.float() - ye.float()).norm() / ye.float().norm()).item()
+            assert err < 1e-3, f"call {i}: compiled vs eager rel-L2 {err:.2e}"
+            outs.append(yc)
+    diffs = [(outs[i] - outs[i + 1]).abs().max().item() for i in range(4)]
+    assert all(d > 0 for d in diffs)

@@ -64,6 +64,18 @@ def test_fake_impls_keep_channels_last(eng, op, args):
         assert y.shape == x.shape and y.stride() == x.stride() and y.dtype == torch.float16
 
 
+def test_bias_act_affine_op_fake_impl(eng):
+    """The pointwise-epilogue op traces under FakeTensorMode (what torch.compile needs) and keeps
+    channels_last strides."""
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    with FakeTensorMode():
+        x = torch.empty((1, 1536, 32, 32), dtype=torch.float16, device="cuda").contiguous(
+            memory_format=torch.channels_last)
+        v = torch.empty((1536,), dtype=torch.float16, device="cuda")
+        y = torch.ops.depthwise.bias_act_affine(x, v, v, v, 2)
+        assert y.shape == x.shape and y.stride() == x.stride()
+
+
 def test_fake_impl_strides_match_reference_check(eng):
     # the survey verified (1572864, 1, 49152, 1536) for [1, 1536, 32, 32] channels_last
     from torch._subclasses.fake_tensor import FakeTensorMode
