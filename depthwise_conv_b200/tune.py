@@ -8,7 +8,9 @@ graph of back-to-back launches, best of 3) on a proxy batch of at most
 ``--proxy-batch`` images until the per-problem time budget runs out; the
 fastest few are then timed on the full batch (both load schedules, both grid
 modes) and the winner is written to ``csrc/dw_tuned_plans.inc``, which the
-library consults before its cost model (rebuild afterwards).  Results
+library consults before its cost model (rebuild afterwards).  ``--epilogue``
+times the fused op with the epilogue a model uses (the table is keyed by
+shape only, so tune a shape for the epilogue it is mostly run with).  Results
 are also printed as JSON lines.
 """
 from __future__ import annotations
@@ -32,16 +34,32 @@ FIELDS = ("cols_per_thread", "rows_per_thread", "tile_h", "tile_w", "ring_rows",
           "load_schedule")
 
 
+EPILOGUE = {}  # keyword arguments of the fused op while timing (set by --epilogue)
+
+
+def _epilogue_args(x):
+    import torch
+    if not EPILOGUE:
+        return {}
+    C = x.shape[1]
+    v = torch.full((C,), 0.5, dtype=torch.float16, device=x.device)
+    kw = dict(bias=v, scale=v, shift=v, act=EPILOGUE["act"])
+    if EPILOGUE.get("residual"):
+        kw["residual"] = x
+    return kw
+
+
 def time_plan(d, x, w, y, plan, accum, reps):
     import torch
     s = torch.cuda.Stream()
+    kw = _epilogue_args(x)
     with torch.cuda.stream(s):
-        d.conv2d_nhwc_fused(x, w, out=y, plan=plan, accum=accum)
+        d.conv2d_nhwc_fused(x, w, out=y, plan=plan, accum=accum, **kw)
         s.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=s):
             for _ in range(reps):
-                d.conv2d_nhwc_fused(x, w, out=y, plan=plan, accum=accum)
+                d.conv2d_nhwc_fused(x, w, out=y, plan=plan, accum=accum, **kw)
     g.replay()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -142,11 +160,15 @@ def main():
     ap.add_argument("--accum", choices=["mixed", "f32"], default="mixed")
     ap.add_argument("--proxy-batch", type=int, default=8, help="images per timing while ranking candidates")
     ap.add_argument("--finalists", type=int, default=8, help="plans re-timed on the full batch")
+    ap.add_argument("--epilogue", choices=["none", "gelu_bn", "gelu_bn_res"], default="none",
+                    help="time with the fused epilogue a model uses (bias+GELU+BN, + residual = input)")
     ap.add_argument("--no-write", action="store_true")
     ap.add_argument("--out", default=TABLE, help="where to write the merged table (default: the library's)")
     args = ap.parse_args()
     from depthwise_conv_b200 import _lib
     accum = _lib.ACCUM_MIXED if args.accum == "mixed" else _lib.ACCUM_F32
+    if args.epilogue != "none":
+        EPILOGUE.update(act="gelu", residual=args.epilogue == "gelu_bn_res")
     probs = [tuple(int(v) for v in p.split(",")) for p in args.problems] or DEFAULT_PROBLEMS
     rows = []
     for B, H, W, C, K in probs:
