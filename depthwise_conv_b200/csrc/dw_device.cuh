@@ -181,7 +181,6 @@ __device__ __forceinline__ f32x2 h2_to_f32x2(__half2 h) {
   return r;
 }
 
-__device__ __forceinline__ float2 f32x2_unpack(f32x2 v) { return bits_f2(v); }
 
 // acc.{lo,hi} += h.{lo,hi} with mixed-precision adds (fp16 operand, fp32
 // accumulator, one rounding each).
@@ -217,24 +216,11 @@ __device__ __forceinline__ float ex2_approx(float x) {
 //   erfc(a) = (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-a^2),
 //   t = 1 / (1 + p a),  |error| <= 1.5e-7,
 // used directly on the negative side (where the product is small and its
-// relative accuracy matters) and as 1 - erfc on the positive side.  About a
-// dozen instructions, two on the special-function unit; the result is within
-// one fp16 ulp of the exact GELU over the whole fp16 range.
-__device__ __forceinline__ float gelu_erf(float v) {
-  const float a = fabsf(v) * 0.70710678118654752f;  // |v| / sqrt(2)
-  const float t = rcp_approx(fmaf(0.3275911f, a, 1.0f));
-  float poly = fmaf(1.061405429f, t, -1.453152027f);
-  poly = fmaf(poly, t, 1.421413741f);
-  poly = fmaf(poly, t, -0.284496736f);
-  poly = fmaf(poly, t, 0.254829592f);
-  poly *= t;
-  const float ec = poly * ex2_approx(-a * a * 1.4426950408889634f);  // erfc(a)
-  const float hv = 0.5f * v;
-  return v >= 0.0f ? fmaf(-hv, ec, v) : hv * ec;  // v (1 - erfc/2)  |  v erfc / 2
-}
-
-// The same GELU on a packed pair: the polynomial and the products run as
-// fp32x2 instructions, only the reciprocal and the exponential per lane.
+// relative accuracy matters) and as 1 - erfc on the positive side.  Evaluated
+// on a packed pair of channels: the polynomial and the products run as fp32x2
+// instructions, only the reciprocal and the exponential per lane (two
+// special-function ops per value); the result is within one fp16 ulp of the
+// exact GELU over the whole fp16 range.
 __device__ __forceinline__ f32x2 gelu_erf2(f32x2 v) {
   const f32x2 a = fmul2(v & 0x7fffffff7fffffffull, splat2(0.70710678118654752f));  // |v| / sqrt(2)
   const float2 d = bits_f2(fma2(a, splat2(0.3275911f), splat2(1.0f)));
@@ -250,12 +236,6 @@ __device__ __forceinline__ f32x2 gelu_erf2(f32x2 v) {
   const float2 pos = bits_f2(fma2(q, splat2(-1.0f), v));  // v (1 - erfc/2)
   const float2 vf = bits_f2(v), qf = bits_f2(q);
   return f2_bits(make_float2(vf.x >= 0.0f ? pos.x : qf.x, vf.y >= 0.0f ? pos.y : qf.y));
-}
-
-__device__ __forceinline__ float apply_act(float v, int act) {
-  if (act == kActRelu) return fmaxf(v, 0.0f);
-  if (act == kActGelu) return gelu_erf(v);
-  return v;
 }
 
 }  // namespace dwb
