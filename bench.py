@@ -23,8 +23,9 @@ One JSON line (rank 0):
   cpu_baseline  the reference's CPU path (fp32 PyTorch ConvMixer, depthwise
             via conv2d(groups=C)) timed on this host's cores, rank 0, N=1
 
---impl reference times that CPU path alone (the reference has no runnable
-GPU path on B200 here) with the same metric and config.
+--impl reference times that CPU path alone (the reference's own GPU ops are
+not an installable package, and its tier here is the CPU path) with the same
+metric and config.
 """
 from __future__ import annotations
 

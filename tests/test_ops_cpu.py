@@ -77,7 +77,8 @@ def test_bias_act_affine_op_fake_impl(eng):
 
 
 def test_fake_impl_strides_match_reference_check(eng):
-    # the survey verified (1572864, 1, 49152, 1536) for [1, 1536, 32, 32] channels_last
+    # the reference's own fake impl gives strides (1572864, 1, 49152, 1536) for a
+    # [1, 1536, 32, 32] channels_last input
     from torch._subclasses.fake_tensor import FakeTensorMode
     with FakeTensorMode():
         x = torch.empty(1, 1536, 32, 32, dtype=torch.float16, device="cuda").contiguous(
