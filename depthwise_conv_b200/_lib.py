@@ -83,6 +83,9 @@ SIGNATURES = {
     "dwb_device_error": ([ctypes.POINTER(ctypes.c_int), _i, _p], _i),
     "dwb_probe_fma_peak": ([ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double), _p], _i),
     "dwb_selftest_bounded_wait": ([_i64, _p], _i),
+    "dwb_weight_rot180": ([_p, _p, _i64, _i, _p], _i),
+    "dwb_conv2d_nhwc_bwd_data": ([_p, _p, _p, _i64, _i64, _i64, _i64, _i, _p], _i),
+    "dwb_conv2d_nhwc_bwd_weight": ([_p, _p, _p, _i64, _i64, _i64, _i64, _i, _p], _i),
 }
 
 _lib = None

@@ -535,6 +535,14 @@ int dwb_conv2d_nhwc_fwd(const void* x, const void* w, void* y, int64_t B, int64_
                         stream);
 }
 
+int dwb_conv2d_nhwc_bwd_data(const void* dy, const void* w_rot180, void* dx, int64_t B, int64_t H, int64_t W,
+                             int64_t C, int K, void* stream) {
+  // "same" padding with an odd K: the adjoint of the convolution is the convolution with the taps
+  // rotated by 180 degrees, so the forward kernel computes the input gradient.
+  return launch_forward(dy, w_rot180, nullptr, nullptr, nullptr, nullptr, dx, B, H, W, C, K, DWB_ACT_NONE,
+                        DWB_ACCUM_DEFAULT, stream);
+}
+
 int dwb_conv2d_nhwc_fused_fwd(const void* x, const void* w, const void* bias, const void* scale, const void* shift,
                               const void* residual, void* y, int64_t B, int64_t H, int64_t W, int64_t C, int K,
                               int act, int accum, void* stream) {

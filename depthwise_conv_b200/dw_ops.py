@@ -14,6 +14,11 @@ Generic ops (new; the reference only has fixed-shape ops):
   semantics of the reference's fused baseline
   (benchmark_cudnn_fused_e2e.py:44-84,115-134) plus ConvMixer's residual
   (convmixer/convmixer.py:58-59).
+
+``depthwise::conv2d_nhwc`` is differentiable (``torch.library.register_autograd``):
+the input gradient runs the forward kernel on dy with the taps rotated by 180
+degrees, the weight gradient a dedicated kernel accumulating in fp32, the bias
+gradient a channel sum.  The reference's ops are inference-only.
 """
 from __future__ import annotations
 
@@ -138,6 +143,43 @@ def bias_act_affine(x: torch.Tensor, bias=None, scale=None, shift=None, act: int
     return y
 
 
+def weight_rot180(w: torch.Tensor) -> torch.Tensor:
+    """[K, K, C] taps rotated by 180 degrees (the input-gradient filter)."""
+    C = w.shape[2]
+    check_weight(w, C)
+    wr = torch.empty_like(w)
+    with _DeviceGuard(w.device):
+        _lib.call("dwb_weight_rot180", w.data_ptr(), wr.data_ptr(), C, w.shape[0], _stream_of(w))
+    return wr
+
+
+def conv2d_nhwc_backward_input(dy: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """dx of y = conv(x, w): the convolution of dy with the rotated taps."""
+    check_input(dy, "grad_output")
+    B, C, H, W = dy.shape
+    K = check_weight(w, C)
+    wr = weight_rot180(w)
+    dx = torch.empty_like(dy)
+    with _DeviceGuard(dy.device):
+        _lib.call("dwb_conv2d_nhwc_bwd_data", dy.data_ptr(), wr.data_ptr(), dx.data_ptr(), B, H, W, C, K,
+                  _stream_of(dy))
+    return dx
+
+
+def conv2d_nhwc_backward_weight(x: torch.Tensor, dy: torch.Tensor, K: int) -> torch.Tensor:
+    """dw of y = conv(x, w) as [K, K, C] float32 (summed over the batch and the image)."""
+    check_input(x)
+    check_input(dy, "grad_output")
+    if dy.shape != x.shape:
+        raise RuntimeError(f"grad_output shape {tuple(dy.shape)} != input shape {tuple(x.shape)}")
+    B, C, H, W = x.shape
+    dw = torch.zeros((K, K, C), dtype=torch.float32, device=x.device)
+    with _DeviceGuard(x.device):
+        _lib.call("dwb_conv2d_nhwc_bwd_weight", x.data_ptr(), dy.data_ptr(), dw.data_ptr(), B, H, W, C, K,
+                  _stream_of(x))
+    return dw
+
+
 def conv2d_nhwc(x: torch.Tensor, w: torch.Tensor, bias=None) -> torch.Tensor:
     """y = conv(x, w) (+ bias): the plain depthwise convolution."""
     return conv2d_nhwc_fused(x, w, bias=bias)
@@ -184,3 +226,22 @@ def _bias_act_affine_impl(input, bias, scale, shift, act):
 @torch.library.register_fake("depthwise::bias_act_affine")
 def _bias_act_affine_fake(input, bias, scale, shift, act):
     return torch.empty_like(input)
+
+
+def _conv2d_nhwc_setup(ctx, inputs, output):
+    x, w, bias = inputs
+    ctx.save_for_backward(x, w)
+    ctx.has_bias = bias is not None
+
+
+def _conv2d_nhwc_backward(ctx, grad):
+    x, w = ctx.saved_tensors
+    g = grad if grad.is_contiguous(memory_format=torch.channels_last) else grad.contiguous(
+        memory_format=torch.channels_last)
+    dx = conv2d_nhwc_backward_input(g, w) if ctx.needs_input_grad[0] else None
+    dw = conv2d_nhwc_backward_weight(x, g, w.shape[0]).to(w.dtype) if ctx.needs_input_grad[1] else None
+    db = g.float().sum(dim=(0, 2, 3)).to(g.dtype) if ctx.has_bias and ctx.needs_input_grad[2] else None
+    return dx, dw, db
+
+
+torch.library.register_autograd("depthwise::conv2d_nhwc", _conv2d_nhwc_backward, setup_context=_conv2d_nhwc_setup)

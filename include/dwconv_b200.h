@@ -213,6 +213,27 @@ DWB_API int dwb_depthwise_29x29_256_nhwc(const void* input, const void* weight, 
 DWB_API int dwb_depthwise_27x27_512_nhwc(const void* input, const void* weight, const void* bias,
                                  void* output, int B, int C, int H, int W, void* stream);
 
+/* ---- gradients ---------------------------------------------------------------
+ * No counterpart in the reference, whose ops are inference-only
+ * (convmixer/kernels/depthwise_torch_ops.py:157-159).  Same layouts as the
+ * forward: x, dy, dx NHWC fp16; w [K][K][C] fp16. */
+
+/* w_rot180[kh][kw][c] = w[K-1-kh][K-1-kw][c] (C % 8 == 0, 16-byte aligned). */
+DWB_API int dwb_weight_rot180(const void* w, void* w_rot180, int64_t C, int K, void* stream);
+
+/* Input gradient: dx = depthwise conv of dy with w_rot180 (from dwb_weight_rot180);
+ * the forward kernel and plan, mixed accumulation. */
+DWB_API int dwb_conv2d_nhwc_bwd_data(const void* dy, const void* w_rot180, void* dx, int64_t B, int64_t H,
+                                     int64_t W, int64_t C, int K, void* stream);
+
+/* Weight gradient, accumulated in fp32: dw[kh][kw][c] += sum over b, h, w of
+ * dy[b][h][w][c] * x[b][h+kh-K/2][w+kw-K/2][c].  dw is [K][K][C] fp32 (8-byte
+ * aligned); zero it first for a plain gradient.  The summation order (atomic
+ * adds of per-warp partial sums) is not fixed, so results may differ in the
+ * last bits between calls. */
+DWB_API int dwb_conv2d_nhwc_bwd_weight(const void* x, const void* dy, float* dw, int64_t B, int64_t H, int64_t W,
+                                       int64_t C, int K, void* stream);
+
 /* ---- diagnostics ----------------------------------------------------------- */
 
 /* Read (and optionally clear) the device-side error word of the current

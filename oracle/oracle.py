@@ -196,6 +196,33 @@ def dw_forward_numpy(x, w, bias=None, scale=None, shift=None, residual=None, act
     return _epilogue_np(acc, C, bias, scale, shift, residual, act)
 
 
+def dw_backward_numpy(x, w, dy):
+    """float64 gradients of y = conv(x, w) ("same" padding, stride 1), for loss = sum(y * dy).
+
+    The reference is inference-only; these are the adjoints of its forward
+    definition (the tap sum of dw_forward_numpy):
+      dx[b,h,w,c]   = sum_{ki,kj} dy[b, h-ki+p, w-kj+p, c] * w[ki,kj,c]
+      dw[ki,kj,c]   = sum_{b,h,w} dy[b,h,w,c] * x[b, h+ki-p, w+kj-p, c]
+      dbias[c]      = sum_{b,h,w} dy[b,h,w,c]
+    Returns (dx NHWC, dw [K,K,C], dbias [C]).
+    """
+    _check_shapes(x, w)
+    B, H, W, C = x.shape
+    K = w.shape[0]
+    p = K // 2
+    xd = np.zeros((B, H + 2 * p, W + 2 * p, C), np.float64)
+    xd[:, p:p + H, p:p + W, :] = np.asarray(x, np.float64)
+    g = np.asarray(dy, np.float64)
+    wd = np.asarray(w, np.float64)
+    gd = np.zeros_like(xd)  # dy scattered back onto the padded input grid
+    dw = np.zeros((K, K, C), np.float64)
+    for ki in range(K):
+        for kj in range(K):
+            gd[:, ki:ki + H, kj:kj + W, :] += g * wd[ki, kj]
+            dw[ki, kj] = (xd[:, ki:ki + H, kj:kj + W, :] * g).sum(axis=(0, 1, 2))
+    return gd[:, p:p + H, p:p + W, :], dw, g.sum(axis=(0, 1, 2))
+
+
 # ---- torch F.conv2d restatement (the reference's own check) ---------------------
 
 def dw_forward_torch(x, w, bias=None, scale=None, shift=None, residual=None, act="none", dtype="float32",

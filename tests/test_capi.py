@@ -69,6 +69,20 @@ def test_validation_statuses(lib):
     assert g(X, Wt, 0x40001, None, None, None, Y, 1, 8, 8, 64, 7, 0, 0, None) == L.ERR_BAD_ALIGN
 
 
+def test_gradient_entry_points_validate(lib):
+    """Shape, pointer and alignment checks of the gradient entry points answer without a device."""
+    from depthwise_conv_b200 import _lib as L
+    X, Y = ctypes.c_void_p(256), ctypes.c_void_p(512)
+    assert lib.dwb_conv2d_nhwc_bwd_weight(X, Y, Y, 1, 8, 8, 64, 8, None) == L.ERR_BAD_SHAPE      # even K
+    assert lib.dwb_conv2d_nhwc_bwd_weight(X, Y, Y, 1, 8, 8, 12, 7, None) == L.ERR_BAD_SHAPE      # C % 8
+    assert lib.dwb_conv2d_nhwc_bwd_weight(None, Y, Y, 1, 8, 8, 64, 7, None) == L.ERR_NULL_POINTER
+    assert lib.dwb_conv2d_nhwc_bwd_weight(ctypes.c_void_p(258), Y, Y, 1, 8, 8, 64, 7, None) == L.ERR_BAD_ALIGN
+    assert lib.dwb_conv2d_nhwc_bwd_weight(None, None, None, 0, 8, 8, 64, 7, None) == L.OK         # empty batch
+    assert lib.dwb_weight_rot180(X, Y, 64, 4, None) == L.ERR_BAD_SHAPE
+    assert lib.dwb_weight_rot180(None, Y, 64, 5, None) == L.ERR_NULL_POINTER
+    assert lib.dwb_conv2d_nhwc_bwd_data(X, Y, Y, 1, 8, 8, 64, 6, None) == L.ERR_BAD_SHAPE
+
+
 def test_fixed_shape_launchers_reject_other_shapes(lib):
     from depthwise_conv_b200 import _lib as L
     assert lib.dwb_depthwise_forward_32_768_7(X, Wt, Y, 16, 32, 768, 7, 1, None) == L.ERR_BAD_SHAPE

@@ -1,0 +1,107 @@
+"""Gradients of the depthwise convolution on the GPU (the reference is inference-only).
+
+Checked against the float64 numpy adjoints in oracle/oracle.py, which are
+themselves pinned to PyTorch autograd through F.conv2d(groups=C)
+(tests/test_oracle.py).  The input gradient runs the forward kernel (mixed
+accumulation) and is held to the forward's bar; the weight gradient sums
+B*H*W products per tap in fp32 and is held to a relative 1e-5.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import make_problem
+
+pytestmark = pytest.mark.gpu
+
+MAX_TOL, REL_TOL = 1e-2, 1e-3
+
+
+@pytest.fixture(scope="module")
+def eng():
+    import depthwise_conv_b200 as d
+    return d
+
+
+def to_dev(a):
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    return t.permute(0, 3, 1, 2) if t.dim() == 4 else t
+
+
+def to_host(t):
+    return t.permute(0, 2, 3, 1).contiguous().cpu().numpy() if t.dim() == 4 else t.cpu().numpy()
+
+
+SHAPES = [(2, 19, 21, 72, 7), (1, 9, 30, 64, 31), (3, 5, 11, 64, 9), (1, 14, 14, 512, 27), (2, 1, 1, 8, 1),
+          (2, 23, 17, 136, 13), (1, 3, 40, 16, 29)]
+
+
+def _problem(B, H, W, C, K):
+    x, w = make_problem(500 + K + C, B, H, W, C, K)
+    dy = np.random.default_rng(K + H).standard_normal((B, H, W, C)).astype(np.float16)
+    return x, w, dy
+
+
+@pytest.mark.parametrize("B,H,W,C,K", SHAPES)
+def test_weight_gradient(eng, oracle_mod, B, H, W, C, K):
+    x, w, dy = _problem(B, H, W, C, K)
+    _, dw_exact, _ = oracle_mod.dw_backward_numpy(x, w, dy)
+    dw = eng.dw_ops.conv2d_nhwc_backward_weight(to_dev(x), to_dev(dy), K)
+    torch.cuda.synchronize()
+    got = dw.cpu().numpy().astype(np.float64)
+    scale = np.abs(dw_exact).max() + 1e-30
+    assert np.abs(got - dw_exact).max() <= 1e-5 * scale + 1e-6
+    assert np.linalg.norm(got - dw_exact) <= 1e-5 * np.linalg.norm(dw_exact) + 1e-6
+
+
+@pytest.mark.parametrize("B,H,W,C,K", SHAPES)
+def test_input_gradient(eng, oracle_mod, B, H, W, C, K):
+    x, w, dy = _problem(B, H, W, C, K)
+    dx_exact, _, _ = oracle_mod.dw_backward_numpy(x, w, dy)
+    dx = eng.dw_ops.conv2d_nhwc_backward_input(to_dev(dy), to_dev(w))
+    torch.cuda.synchronize()
+    assert dx.is_contiguous(memory_format=torch.channels_last)
+    max_err, rel = oracle_mod.parity(to_host(dx).astype(np.float64), dx_exact)
+    assert max_err <= MAX_TOL and rel <= REL_TOL, f"max {max_err:.3e} rel {rel:.3e}"
+
+
+def test_weight_gradient_accumulates_into_dw(eng, oracle_mod):
+    """dwb_conv2d_nhwc_bwd_weight adds to dw: two calls give twice the gradient."""
+    from depthwise_conv_b200 import _lib
+    B, H, W, C, K = 2, 12, 12, 64, 9
+    x, w, dy = _problem(B, H, W, C, K)
+    _, dw_exact, _ = oracle_mod.dw_backward_numpy(x, w, dy)
+    xd, gd = to_dev(x), to_dev(dy)
+    dw = torch.zeros((K, K, C), dtype=torch.float32, device="cuda")
+    for _ in range(2):
+        assert _lib.load().dwb_conv2d_nhwc_bwd_weight(xd.data_ptr(), gd.data_ptr(), dw.data_ptr(), B, H, W, C, K,
+                                                      torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    got = dw.cpu().numpy().astype(np.float64)
+    assert np.abs(got - 2 * dw_exact).max() <= 2e-5 * np.abs(dw_exact).max()
+
+
+@pytest.mark.parametrize("with_bias", [True, False])
+def test_autograd_through_the_op(eng, oracle_mod, with_bias):
+    """loss = sum(conv2d_nhwc(x, w, b) * g): x.grad, w.grad, b.grad from the engine's backward."""
+    B, H, W, C, K = 2, 16, 20, 128, 9
+    x, w, dy = _problem(B, H, W, C, K)
+    b = (np.random.default_rng(3).standard_normal(C) * 0.1).astype(np.float16)
+    xt = to_dev(x).requires_grad_()
+    wt = to_dev(w).requires_grad_()
+    bt = to_dev(b).requires_grad_() if with_bias else None
+    y = torch.ops.depthwise.conv2d_nhwc(xt, wt, bt)
+    y.backward(to_dev(dy))
+    torch.cuda.synchronize()
+    dx_exact, dw_exact, db_exact = oracle_mod.dw_backward_numpy(x, w, dy)
+    max_err, rel = oracle_mod.parity(to_host(xt.grad).astype(np.float64), dx_exact)
+    assert max_err <= MAX_TOL and rel <= REL_TOL
+    assert wt.grad.dtype == torch.float16 and wt.grad.shape == (K, K, C)
+    gw = wt.grad.cpu().numpy().astype(np.float64)
+    assert np.abs(gw - dw_exact).max() <= 1e-3 * np.abs(dw_exact).max()  # fp16 rounding of the fp32 sum
+    if with_bias:
+        gb = bt.grad.cpu().numpy().astype(np.float64)
+        assert np.abs(gb - db_exact).max() <= 1e-3 * np.abs(db_exact).max() + 1e-3
+    assert eng.device_error() == 0

@@ -111,3 +111,23 @@ def test_fp16_emulation_distance_grows_with_k(oracle_mod):
         exact, _ = oracle_mod.dw_forward(x, w)
         rels.append(oracle_mod.parity(oracle_mod.dw_forward_f16acc(x, w), exact)[1])
     assert rels[1] > rels[0]
+
+
+@pytest.mark.parametrize("B,H,W,C,K", [(2, 7, 9, 8, 3), (1, 5, 4, 16, 7), (2, 6, 6, 8, 1)])
+def test_backward_restatement_matches_torch_autograd(oracle_mod, B, H, W, C, K):
+    """The numpy gradients agree with PyTorch autograd through F.conv2d(groups=C) in float64."""
+    import torch
+    import torch.nn.functional as F
+    rng = np.random.default_rng(K * 10 + B)
+    x = rng.standard_normal((B, H, W, C)).astype(np.float16)
+    w = (rng.standard_normal((K, K, C)) / K).astype(np.float16)
+    dy = rng.standard_normal((B, H, W, C)).astype(np.float16)
+    dx, dw, db = oracle_mod.dw_backward_numpy(x, w, dy)
+    xt = torch.tensor(x.astype(np.float64)).permute(0, 3, 1, 2).requires_grad_()
+    wt = torch.tensor(w.astype(np.float64)).permute(2, 0, 1).unsqueeze(1).requires_grad_()
+    bt = torch.zeros(C, dtype=torch.float64, requires_grad=True)
+    y = F.conv2d(xt, wt, bt, padding=K // 2, groups=C)
+    y.backward(torch.tensor(dy.astype(np.float64)).permute(0, 3, 1, 2))
+    np.testing.assert_allclose(dx, xt.grad.permute(0, 2, 3, 1).numpy(), rtol=1e-12, atol=1e-12)
+    np.testing.assert_allclose(dw, wt.grad.squeeze(1).permute(1, 2, 0).numpy(), rtol=1e-12, atol=1e-12)
+    np.testing.assert_allclose(db, bt.grad.numpy(), rtol=1e-12, atol=1e-12)
