@@ -644,4 +644,52 @@ int dwb_device_error(int* code_out, int clear, void* stream) {
   return DWB_OK;
 }
 
+// ---- input gradient without any allocation ------------------------------------
+// Some callers cannot allocate device memory at the point where they need the
+// input gradient: code that must not call cudaMalloc there (a serving or
+// training loop whose memory is fixed after warm-up, a host framework that
+// owns every device allocation and exposes no allocator to its plugins).
+// dwb_conv2d_nhwc_bwd_data
+// needs a buffer for the rotated taps that its caller allocates; this variant
+// keeps them in a buffer compiled into the library instead, so it takes the
+// unrotated weights and allocates nothing.
+//
+// The buffer is a file-scope device array: every GPU that loads the library
+// reserves kNoAllocMaxTaps halves (4 MiB) for it until the process exits.  In
+// host code its name is only a stand-in for the device symbol, so its device
+// address is looked up once per device (cudaGetSymbolAddress, the device
+// current) on the first call of this entry point on that device.  All calls
+// share the one buffer: each call overwrites the K*K*C entries it uses before
+// reading them (nothing needs to start at zero), and calls on one device whose
+// work overlaps on the GPU (for example on two streams) race on it: order them.
+constexpr long long kNoAllocMaxTaps = 1LL << 21;  // K*K*C fp16 taps
+static __device__ __align__(256) __half g_noalloc_rot_taps[kNoAllocMaxTaps];
+static std::once_flag g_noalloc_once[kMaxDevices];
+static void* g_noalloc_taps[kMaxDevices];
+static cudaError_t g_noalloc_lookup[kMaxDevices];
+
+int dwb_conv2d_nhwc_bwd_data_noalloc(const void* dy, const void* w, void* dx, int64_t B, int64_t H, int64_t W,
+                                     int64_t C, int K, void* stream) {
+  int rc = validate_args(dy, w, nullptr, nullptr, nullptr, nullptr, dx, B, H, W, C, K, DWB_ACT_NONE,
+                         DWB_ACCUM_DEFAULT);
+  if (rc != DWB_OK) return rc;
+  if (static_cast<long long>(K) * K * C > kNoAllocMaxTaps) {
+    std::snprintf(g_last_error, sizeof(g_last_error),
+                  "dwb_conv2d_nhwc_bwd_data_noalloc: K*K*C = %lld taps exceeds the built-in buffer of %lld",
+                  static_cast<long long>(K) * K * C, kNoAllocMaxTaps);
+    return DWB_ERR_BAD_SHAPE;
+  }
+  if (B == 0) return DWB_OK;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return DWB_ERR_NO_DEVICE;
+  std::call_once(g_noalloc_once[dev], [dev] {
+    g_noalloc_lookup[dev] = cudaGetSymbolAddress(&g_noalloc_taps[dev], g_noalloc_rot_taps);
+  });
+  if (g_noalloc_lookup[dev] != cudaSuccess) return cuda_fail("cudaGetSymbolAddress(g_noalloc_rot_taps)", g_noalloc_lookup[dev]);
+  rc = dwb_weight_rot180(w, g_noalloc_taps[dev], C, K, stream);
+  if (rc != DWB_OK) return rc;
+  return launch_forward(dy, g_noalloc_taps[dev], nullptr, nullptr, nullptr, nullptr, dx, B, H, W, C, K, DWB_ACT_NONE,
+                        DWB_ACCUM_DEFAULT, stream);
+}
+
 }  // extern "C"

@@ -234,6 +234,20 @@ DWB_API int dwb_conv2d_nhwc_bwd_data(const void* dy, const void* w_rot180, void*
 DWB_API int dwb_conv2d_nhwc_bwd_weight(const void* x, const void* dy, float* dw, int64_t B, int64_t H, int64_t W,
                                        int64_t C, int K, void* stream);
 
+/* Input gradient that allocates nothing (no counterpart in the reference): the
+ * same result as dwb_weight_rot180 + dwb_conv2d_nhwc_bwd_data, for callers
+ * that cannot allocate device memory where they need it (a serving loop with
+ * memory fixed after warm-up, a framework that owns every allocation).  Takes
+ * the unrotated w; the rotated taps go to a 4 MiB buffer built into the
+ * library (every GPU that loads the library holds it until exit), so K*K*C
+ * must be at most 2097152 (DWB_ERR_BAD_SHAPE and a dwb_last_error message
+ * otherwise).  The first call on a device looks up the buffer's address
+ * (cudaGetSymbolAddress): make that first call before any stream capture.
+ * All calls share the buffer: calls on one device whose work overlaps on the
+ * GPU race on it. */
+DWB_API int dwb_conv2d_nhwc_bwd_data_noalloc(const void* dy, const void* w, void* dx, int64_t B, int64_t H,
+                                             int64_t W, int64_t C, int K, void* stream);
+
 /* ---- diagnostics ----------------------------------------------------------- */
 
 /* Read (and optionally clear) the device-side error word of the current
