@@ -63,6 +63,8 @@ def parse_args():
     ap.add_argument("--epilogue", choices=["none", "gelu_bn"], default="gelu_bn",
                     help="dw workload: plain conv, or the fused bias+GELU+BN-scale/shift epilogue")
     ap.add_argument("--accum", choices=["mixed", "f32"], default="mixed")
+    ap.add_argument("--backward", action="store_true",
+                    help="--workload dw: also time the layer's gradients (input and weight), warm protocol")
     return ap.parse_args()
 
 
@@ -437,10 +439,52 @@ def run_dw(args):
                 best = min(best, e0.elapsed_time(e1) / reps)
         del g
         warm_us = best * 1000.0
+
+    def warm_time(fn, reps=20):
+        with torch.cuda.stream(stream):
+            fn()
+            stream.synchronize()
+            gb = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gb, stream=stream):
+                for _ in range(reps):
+                    fn()
+            gb.replay()
+            stream.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            best = 1e30
+            for _ in range(3):
+                e0.record(stream)
+                gb.replay()
+                e1.record(stream)
+                stream.synchronize()
+                best = min(best, e0.elapsed_time(e1) / reps)
+        del gb
+        return best * 1000.0
+
+    bwd = None
+    if args.backward and B:
+        dy = torch.randn(x.shape, generator=torch.Generator().manual_seed(1)).half().to(dev).contiguous(
+            memory_format=torch.channels_last)
+        w_rot = torch.empty_like(w)
+        dx = torch.empty_like(x)
+        dw = torch.zeros((K, K, C), dtype=torch.float32, device=dev)
+        s_ = lambda: stream.cuda_stream  # noqa: E731
+
+        def bwd_input():
+            _lib.call("dwb_weight_rot180", w.data_ptr(), w_rot.data_ptr(), C, K, s_())
+            _lib.call("dwb_conv2d_nhwc_bwd_data", dy.data_ptr(), w_rot.data_ptr(), dx.data_ptr(), B, H, W, C, K, s_())
+
+        def bwd_weight():
+            dw.zero_()
+            _lib.call("dwb_conv2d_nhwc_bwd_weight", x.data_ptr(), dy.data_ptr(), dw.data_ptr(), B, H, W, C, K, s_())
+
+        bwd = {"input_us": warm_time(bwd_input), "weight_us": warm_time(bwd_weight)}
     if world > 1:
         dist.barrier()
     ms_max = max_over_ranks(ms, dev)
     warm_max = max_over_ranks(warm_us if warm_us is not None else 0.0, dev)
+    if args.backward:
+        bwd = {k: max_over_ranks(bwd[k] if bwd else 0.0, dev) for k in ("input_us", "weight_us")}
     us_layer = ms_max * 1000.0 / args.steps
     hfma2_tf, ffma2_tf = dwb.probe_fma_peak(stream.cuda_stream)
     if world > 1:
@@ -449,7 +493,7 @@ def run_dw(args):
         return
     fl = valid_flops(Bg, H, W, C, K)
     by = dw_bytes(Bg, H, W, C, K, epilogue=False) + (3 * 2 * C if epi else 0)
-    achieved = fl / (us_layer * 1e-6) / 1e12
+    achieved = fl / world / (us_layer * 1e-6) / 1e12  # per GPU: each rank's launch covers its batch shard
     peaks = measured_peaks()
     plan = _lib.plan_select(max(1, -(-Bg // world)), H, W, C, K, accum)
     line = {
@@ -460,17 +504,22 @@ def run_dw(args):
         "data": "synthetic x ~ N(0,1), w ~ N(0,1/k^2), seeded",
         "config": {"workload": "depthwise layer", "B": Bg, "H": H, "W": W, "C": C, "K": K,
                    "epilogue": args.epilogue, "images_per_s": Bg / (us_layer * 1e-6),
-                   "warm_us_per_layer": warm_max, "warm_fma_frac": (fl / (warm_max * 1e-6) / 1e12 / hfma2_tf)
+                   "warm_us_per_layer": warm_max, "warm_fma_frac": (fl / world / (warm_max * 1e-6) / 1e12 / hfma2_tf)
                    if warm_max > 0 else None,
+                   "backward": None if not args.backward else {
+                       "input_grad_us": bwd["input_us"], "weight_grad_us": bwd["weight_us"],
+                       "input_grad_fma_frac": fl / world / (bwd["input_us"] * 1e-6) / 1e12 / hfma2_tf,
+                       "weight_grad_fma_frac": fl / world / (bwd["weight_us"] * 1e-6) / 1e12 / hfma2_tf,
+                       "protocol": "warm, CUDA graph of 20 launches; dy ~ N(0,1); same valid FLOPs as the forward"},
                    "parallelism": f"batch-sharded x{world}, no collectives",
                    "l2": "flushed (256 MB write) between timed iterations",
                    "plan": {k: plan[k] for k in ("cols_per_thread", "rows_per_thread", "tile_h", "tile_w",
                                                  "consumer_warps", "accum")}},
         "roofline": {"bound": "fma", "achieved": achieved, "peak": hfma2_tf, "unit": "TFLOP/s",
-                     "frac": achieved / hfma2_tf, "flops_per_launch": fl,
+                     "frac": achieved / hfma2_tf, "flops_per_launch": fl / world,
                      "traffic": profiled_traffic().get(f"dw_{Bg}_{H}_{W}_{C}_{K}"),
                      "peak_source": "measured in this run: CUDA-core HFMA2 microbenchmark",
-                     "hbm": {"achieved": by / (us_layer * 1e-6) / 1e9, "peak": peaks.get("hbm_gbs"), "unit": "GB/s",
+                     "hbm": {"achieved": by / world / (us_layer * 1e-6) / 1e9, "peak": peaks.get("hbm_gbs"), "unit": "GB/s",
                              "bytes_per_launch": by}},
         "gpu_launches": args.steps,  # the timed (cold) loop; the warm graph is timed separately
         "clocks": clk,

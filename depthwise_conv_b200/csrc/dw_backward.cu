@@ -8,13 +8,14 @@
 //                   dy[b][h][w][c] * x[b][h + kh - K/2][w + kw - K/2][c]
 //                   (this file).
 //
-// Weight gradient decomposition: a warp owns one kernel row kh, 64 channels
-// (lane = channel pair) and a chunk of output rows (b, h).  For each output
-// row it slides along the row in blocks of R columns: R dy values and the
-// R + K - 1 x values they meet are read (coalesced 128-byte rows per warp,
-// converted to fp32), and the R x K products go into K packed fp32
-// accumulators, one per kw.  At the end the warp adds its K x 64 partial sums
-// into dw with fp32 atomics, so the result needs no buffer beyond dw itself
+// Weight gradient decomposition: a warp owns one kernel row kh (for K > 13
+// half of its taps), 64 channels (lane = channel pair) and a chunk of output
+// rows (b, h).  For each output row it slides along the row in blocks of R
+// columns: R dy values and the R + KW - 1 x values they meet are read
+// (coalesced 128-byte rows per warp, converted to fp32), and the R x KW
+// products go into KW packed fp32 accumulators, one per tap.  At the end the
+// warp adds its KW x 64 partial sums into dw with fp32 atomics, so the result
+// needs no buffer beyond dw itself
 // (the caller zeroes dw, or passes a sum to add to).  Chunks are sized so the
 // grid holds at least ~16 warps per SM.
 #include <cuda_fp16.h>
@@ -29,8 +30,16 @@ namespace dwb {
 constexpr int kWgradR = 16;      // output columns per register block
 constexpr int kWgradWarps = 4;   // warps (chunks) per CTA
 
+// KW taps of the kernel row per warp (kw0 = blockIdx.y % nkw * KW): large K
+// splits the row over warps, which halves each warp's accumulators and x reads
+// and lets more warps share an SM.
 template <int K>
-__global__ void __launch_bounds__(kWgradWarps * 32) dw_wgrad_kernel(const __half2* __restrict__ x,
+constexpr int wgrad_kw() {
+  return K <= 13 ? K : (K + 1) / 2;
+}
+
+template <int K>
+__global__ void __launch_bounds__(kWgradWarps * 32, 4) dw_wgrad_kernel(const __half2* __restrict__ x,
                                                                     const __half2* __restrict__ dy,
                                                                     float* __restrict__ dw, int B, int H, int W,
                                                                     int C, long long rows_per_chunk,
@@ -39,10 +48,13 @@ __global__ void __launch_bounds__(kWgradWarps * 32) dw_wgrad_kernel(const __half
   griddep_wait();  // x and dy may come from the previous kernel
   constexpr int PAD = K / 2;
   constexpr int R = kWgradR;
-  constexpr int NJ = R + K - 1;
+  constexpr int KW = wgrad_kw<K>();
+  constexpr int NKW = (K + KW - 1) / KW;
+  constexpr int NJ = R + KW - 1;
   const int lane = threadIdx.x & 31;
   const long long chunk = static_cast<long long>(blockIdx.z) * kWgradWarps + (threadIdx.x >> 5);
-  const int kh = blockIdx.y;
+  const int kh = blockIdx.y / NKW;
+  const int kw0 = (blockIdx.y - kh * NKW) * KW;
   const int c = blockIdx.x * 64 + 2 * lane;  // this lane's channel pair
   if (chunk >= nchunks || c >= C) return;
   const int C2 = C / 2;  // half2 per pixel
@@ -50,9 +62,9 @@ __global__ void __launch_bounds__(kWgradWarps * 32) dw_wgrad_kernel(const __half
   const long long r0 = chunk * rows_per_chunk;
   const long long r1 = r0 + rows_per_chunk < rows ? r0 + rows_per_chunk : rows;
 
-  f32x2 acc[K];
+  f32x2 acc[KW];
 #pragma unroll
-  for (int kw = 0; kw < K; ++kw) acc[kw] = f32x2_zero();
+  for (int k = 0; k < KW; ++k) acc[k] = f32x2_zero();
 
   for (long long r = r0; r < r1; ++r) {
     const int b = static_cast<int>(r / H);
@@ -70,22 +82,23 @@ __global__ void __launch_bounds__(kWgradWarps * 32) dw_wgrad_kernel(const __half
       }
 #pragma unroll
       for (int j = 0; j < NJ; ++j) {
-        const int iw = w0 + j - PAD;
+        const int iw = w0 + kw0 + j - PAD;
         const f32x2 xv = (iw >= 0 && iw < W) ? h2_to_f32x2(xrow[static_cast<long long>(iw) * C2]) : f32x2_zero();
 #pragma unroll
         for (int i = 0; i < R; ++i) {
-          const int kw = j - i;
-          if (kw >= 0 && kw < K) ffma2(acc[kw], dv[i], xv);
+          const int k = j - i;
+          if (k >= 0 && k < KW) ffma2(acc[k], dv[i], xv);
         }
       }
     }
   }
   float* out = dw + static_cast<long long>(kh) * K * C + c;
 #pragma unroll
-  for (int kw = 0; kw < K; ++kw) {
-    const float2 v = bits_f2(acc[kw]);
-    atomicAdd(out + static_cast<long long>(kw) * C, v.x);
-    atomicAdd(out + static_cast<long long>(kw) * C + 1, v.y);
+  for (int k = 0; k < KW; ++k) {
+    if (kw0 + k >= K) break;  // the last warp of an odd row has one tap fewer
+    const float2 v = bits_f2(acc[k]);
+    atomicAdd(out + static_cast<long long>(kw0 + k) * C, v.x);
+    atomicAdd(out + static_cast<long long>(kw0 + k) * C + 1, v.y);
   }
 }
 
@@ -104,6 +117,12 @@ __global__ void weight_rot180_kernel(const uint4* __restrict__ w, uint4* __restr
 template <int K>
 const void* wgrad_fn() {
   return reinterpret_cast<const void*>(&dw_wgrad_kernel<K>);
+}
+
+// Warps per kernel row (the kw split of wgrad_kw) for a runtime K.
+static int wgrad_nkw(int K) {
+  const int kw = K <= 13 ? K : (K + 1) / 2;
+  return (K + kw - 1) / kw;
 }
 
 static const void* wgrad_for(int K) {
@@ -138,7 +157,8 @@ extern "C" int dwb_conv2d_nhwc_bwd_weight(const void* x, const void* dy, float* 
   const long long rows = B * H;
   const long long cblocks = (C + 63) / 64;
   // at least ~16 warps per SM over (channel block, kernel row, chunk)
-  const long long want = (16LL * sms + cblocks * K - 1) / (cblocks * K);
+  const long long rowsets = cblocks * K * wgrad_nkw(K);  // (channel block, kernel row, kw part)
+  const long long want = (16LL * sms + rowsets - 1) / rowsets;
   const long long nchunks = want < rows ? (want > 0 ? want : 1) : rows;
   const long long rows_per_chunk = (rows + nchunks - 1) / nchunks;
   const long long nchunks_used = (rows + rows_per_chunk - 1) / rows_per_chunk;
@@ -149,7 +169,8 @@ extern "C" int dwb_conv2d_nhwc_bwd_weight(const void* x, const void* dy, float* 
   int Bi = static_cast<int>(B), Hi = static_cast<int>(H), Wi = static_cast<int>(W), Ci = static_cast<int>(C);
   long long rpc = rows_per_chunk, nch = nchunks_used;
   void* args[9] = {&xp, &dyp, &dw, &Bi, &Hi, &Wi, &Ci, &rpc, &nch};
-  const cudaError_t e = launch_kernel(wgrad_for(K), dim3(static_cast<unsigned>(cblocks), K, static_cast<unsigned>(zblocks)),
+  const cudaError_t e = launch_kernel(wgrad_for(K),
+                                      dim3(static_cast<unsigned>(cblocks), K * wgrad_nkw(K), static_cast<unsigned>(zblocks)),
                                       dim3(kWgradWarps * 32), args, 0, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) {
     (void)cudaGetLastError();
