@@ -8,97 +8,132 @@
 //                   dy[b][h][w][c] * x[b][h + kh - K/2][w + kw - K/2][c]
 //                   (this file).
 //
-// Weight gradient decomposition: a warp owns one kernel row kh (for K > 13
-// half of its taps), 64 channels (lane = channel pair) and a chunk of output
-// rows (b, h).  For each output row it slides along the row in blocks of R
-// columns: R dy values and the R + KW - 1 x values they meet are read
-// (coalesced 128-byte rows per warp, converted to fp32), and the R x KW
-// products go into KW packed fp32 accumulators, one per tap.  At the end the
-// warp adds its KW x 64 partial sums into dw with fp32 atomics, so the result
-// needs no buffer beyond dw itself
-// (the caller zeroes dw, or passes a sum to add to).  Chunks are sized so the
-// grid holds at least ~16 warps per SM.
+// Weight gradient decomposition: one CTA per (64-channel block, kernel row
+// kh, column tile, chunk of output rows).  A producer warp streams, for every
+// output row h of the chunk whose input row ih = h + kh - K/2 lies in the
+// image, one stage holding the dy row segment (tile_w columns) and the x row
+// segment it meets (tile_w + K - 1 columns, zero outside the image from the
+// TMA fill) through a ring of shared-memory stages with full/empty mbarriers
+// (bounded waits), like the forward kernel.  Each consumer warp owns R = 16
+// columns of the tile (lane = channel pair): per stage it converts its R dy
+// values and R + K - 1 x values to fp32 and adds the R x K products into K
+// packed fp32 accumulators, one per kw.  At the end it adds them into dw with
+// fp32 atomics, so the result needs no buffer beyond dw itself (the caller
+// zeroes dw, or passes a sum to add to).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "../../include/dwconv_b200.h"
+#include "dw_backward.h"
 #include "dw_device.cuh"
 #include "dw_launch.h"
 
 namespace dwb {
 
-constexpr int kWgradR = 16;      // output columns per register block
-constexpr int kWgradWarps = 4;   // warps (chunks) per CTA
-
-// KW taps of the kernel row per warp (kw0 = blockIdx.y % nkw * KW): large K
-// splits the row over warps, which halves each warp's accumulators and x reads
-// and lets more warps share an SM.
-template <int K>
-constexpr int wgrad_kw() {
-  return K <= 13 ? K : (K + 1) / 2;
-}
+constexpr int kWgradR = 16;  // output columns per consumer warp
 
 template <int K>
-__global__ void __launch_bounds__(kWgradWarps * 32, 4) dw_wgrad_kernel(const __half2* __restrict__ x,
-                                                                    const __half2* __restrict__ dy,
-                                                                    float* __restrict__ dw, int B, int H, int W,
-                                                                    int C, long long rows_per_chunk,
-                                                                    long long nchunks) {
-  griddep_launch_dependents();
-  griddep_wait();  // x and dy may come from the previous kernel
+__global__ void __launch_bounds__(160, 1) dw_wgrad_kernel(const __grid_constant__ CUtensorMap tm_x,
+                                                          const __grid_constant__ CUtensorMap tm_dy,
+                                                          const WgradParams p) {
   constexpr int PAD = K / 2;
   constexpr int R = kWgradR;
-  constexpr int KW = wgrad_kw<K>();
-  constexpr int NKW = (K + KW - 1) / KW;
-  constexpr int NJ = R + KW - 1;
+  constexpr int NJ = R + K - 1;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  const int NS = p.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + NS;
+  unsigned char* ring = smem + p.ring_off;
+  const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const long long chunk = static_cast<long long>(blockIdx.z) * kWgradWarps + (threadIdx.x >> 5);
-  const int kh = blockIdx.y / NKW;
-  const int kw0 = (blockIdx.y - kh * NKW) * KW;
-  const int c = blockIdx.x * 64 + 2 * lane;  // this lane's channel pair
-  if (chunk >= nchunks || c >= C) return;
-  const int C2 = C / 2;  // half2 per pixel
-  const long long rows = static_cast<long long>(B) * H;
-  const long long r0 = chunk * rows_per_chunk;
-  const long long r1 = r0 + rows_per_chunk < rows ? r0 + rows_per_chunk : rows;
+  const uint32_t dy_bytes = static_cast<uint32_t>(p.tile_w) * 128u;
+  const uint32_t x_bytes = static_cast<uint32_t>(p.tile_w + K - 1) * 128u;
 
-  f32x2 acc[KW];
-#pragma unroll
-  for (int k = 0; k < KW; ++k) acc[k] = f32x2_zero();
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tm_x);
+    prefetch_tmap(&tm_dy);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], p.consumer_warps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  griddep_launch_dependents();
+  griddep_wait();  // x and dy may come from the previous kernel
 
-  for (long long r = r0; r < r1; ++r) {
-    const int b = static_cast<int>(r / H);
-    const int h = static_cast<int>(r - static_cast<long long>(b) * H);
-    const int ih = h + kh - PAD;
-    if (ih < 0 || ih >= H) continue;  // warp-uniform
-    const __half2* dyrow = dy + (static_cast<long long>(b) * H + h) * W * C2 + c / 2;
-    const __half2* xrow = x + (static_cast<long long>(b) * H + ih) * W * C2 + c / 2;
-    for (int w0 = 0; w0 < W; w0 += R) {
-      f32x2 dv[R];
-#pragma unroll
-      for (int i = 0; i < R; ++i) {
-        const int w = w0 + i;
-        dv[i] = w < W ? h2_to_f32x2(dyrow[static_cast<long long>(w) * C2]) : f32x2_zero();
-      }
-#pragma unroll
-      for (int j = 0; j < NJ; ++j) {
-        const int iw = w0 + kw0 + j - PAD;
-        const f32x2 xv = (iw >= 0 && iw < W) ? h2_to_f32x2(xrow[static_cast<long long>(iw) * C2]) : f32x2_zero();
-#pragma unroll
-        for (int i = 0; i < R; ++i) {
-          const int k = j - i;
-          if (k >= 0 && k < KW) ffma2(acc[k], dv[i], xv);
-        }
+  const int c0 = blockIdx.x * 64;
+  const int kh = blockIdx.y;
+  const int ct = static_cast<int>(blockIdx.z % static_cast<unsigned>(p.col_tiles));
+  const long long chunk = blockIdx.z / static_cast<unsigned>(p.col_tiles);
+  const int w0 = ct * p.tile_w;
+  const long long rows = static_cast<long long>(p.B) * p.H;
+  const long long r0 = chunk * p.rows_per_chunk;
+  const long long r1 = r0 + p.rows_per_chunk < rows ? r0 + p.rows_per_chunk : rows;
+
+  if (warp == p.consumer_warps) {
+    // ---- producer: one stage per output row with an in-image input row ----
+    if (lane == 0) {
+      RingPos fr;
+      long long fills = 0;
+      for (long long r = r0; r < r1; ++r) {
+        const int b = static_cast<int>(r / p.H);
+        const int h = static_cast<int>(r - static_cast<long long>(b) * p.H);
+        const int ih = h + kh - PAD;
+        if (ih < 0 || ih >= p.H) continue;
+        if (fills >= NS && !mbar_wait_bounded<true>(&empty[fr.slot], fr.phase ^ 1u, p.err, 3)) break;
+        unsigned char* dst = ring + fr.slot * p.stage_bytes;
+        mbar_arrive_expect_tx(&full[fr.slot], dy_bytes + x_bytes);
+        tma_load_4d(dst, &tm_dy, &full[fr.slot], c0, w0, h, b);
+        tma_load_4d(dst + dy_bytes, &tm_x, &full[fr.slot], c0, w0 - PAD, ih, b);
+        fr.next(NS);
+        ++fills;
       }
     }
+    return;
   }
-  float* out = dw + static_cast<long long>(kh) * K * C + c;
+
+  // ---- consumers: R columns each, K accumulators per channel pair ----
+  const int col0 = warp * R;
+  f32x2 acc[K];
 #pragma unroll
-  for (int k = 0; k < KW; ++k) {
-    if (kw0 + k >= K) break;  // the last warp of an odd row has one tap fewer
-    const float2 v = bits_f2(acc[k]);
-    atomicAdd(out + static_cast<long long>(kw0 + k) * C, v.x);
-    atomicAdd(out + static_cast<long long>(kw0 + k) * C + 1, v.y);
+  for (int k = 0; k < K; ++k) acc[k] = f32x2_zero();
+  RingPos ws;
+  bool ok = true;
+  for (long long r = r0; r < r1 && ok; ++r) {
+    const int b = static_cast<int>(r / p.H);
+    const int h = static_cast<int>(r - static_cast<long long>(b) * p.H);
+    const int ih = h + kh - PAD;
+    if (ih < 0 || ih >= p.H) continue;  // the producer skipped it too
+    ok = mbar_wait_bounded(&full[ws.slot], ws.phase, p.err, 2);
+    if (!ok) break;
+    const unsigned char* st = ring + ws.slot * p.stage_bytes;
+    const __half2* dyr = reinterpret_cast<const __half2*>(st) + col0 * 32 + lane;
+    const __half2* xr = reinterpret_cast<const __half2*>(st + dy_bytes) + col0 * 32 + lane;
+    f32x2 dv[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) dv[i] = h2_to_f32x2(dyr[i * 32]);
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      const f32x2 xv = h2_to_f32x2(xr[j * 32]);
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        const int kw = j - i;
+        if (kw >= 0 && kw < K) ffma2(acc[kw], dv[i], xv);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[ws.slot]);
+    ws.next(NS);
+  }
+  const int c = c0 + 2 * lane;
+  if (!ok || c >= p.C) return;
+  float* out = p.dw + static_cast<long long>(kh) * K * p.C + c;
+#pragma unroll
+  for (int kw = 0; kw < K; ++kw) {
+    const float2 v = bits_f2(acc[kw]);
+    atomicAdd(out + static_cast<long long>(kw) * p.C, v.x);
+    atomicAdd(out + static_cast<long long>(kw) * p.C + 1, v.y);
   }
 }
 
@@ -119,13 +154,7 @@ const void* wgrad_fn() {
   return reinterpret_cast<const void*>(&dw_wgrad_kernel<K>);
 }
 
-// Warps per kernel row (the kw split of wgrad_kw) for a runtime K.
-static int wgrad_nkw(int K) {
-  const int kw = K <= 13 ? K : (K + 1) / 2;
-  return (K + kw - 1) / kw;
-}
-
-static const void* wgrad_for(int K) {
+const void* wgrad_kernel_for(int K) {
   switch (K) {
 #define DWB_WG(KK) \
   case KK:         \
@@ -141,43 +170,6 @@ static const void* wgrad_for(int K) {
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace dwb
-
-extern "C" int dwb_conv2d_nhwc_bwd_weight(const void* x, const void* dy, float* dw, int64_t B, int64_t H, int64_t W,
-                                          int64_t C, int K, void* stream) {
-  using namespace dwb;
-  if (B < 0 || H < 1 || W < 1 || C < 8 || (C % 8) != 0 || K < 1 || K > 31 || (K % 2) == 0)
-    return DWB_ERR_BAD_SHAPE;
-  if (H > (1 << 30) || W > (1 << 30) || C > (1 << 30) || B > (1 << 30)) return DWB_ERR_BAD_SHAPE;
-  if (B == 0) return DWB_OK;
-  if (!x || !dy || !dw) return DWB_ERR_NULL_POINTER;
-  if (!aligned16(x) || !aligned16(dy) || (reinterpret_cast<uintptr_t>(dw) & 7u) != 0) return DWB_ERR_BAD_ALIGN;
-  int dev = 0, sms = 148;
-  if (cudaGetDevice(&dev) != cudaSuccess) return DWB_ERR_NO_DEVICE;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const long long rows = B * H;
-  const long long cblocks = (C + 63) / 64;
-  // at least ~16 warps per SM over (channel block, kernel row, chunk)
-  const long long rowsets = cblocks * K * wgrad_nkw(K);  // (channel block, kernel row, kw part)
-  const long long want = (16LL * sms + rowsets - 1) / rowsets;
-  const long long nchunks = want < rows ? (want > 0 ? want : 1) : rows;
-  const long long rows_per_chunk = (rows + nchunks - 1) / nchunks;
-  const long long nchunks_used = (rows + rows_per_chunk - 1) / rows_per_chunk;
-  const long long zblocks = (nchunks_used + kWgradWarps - 1) / kWgradWarps;
-  if (cblocks > 0x7fffffffLL || zblocks > 65535) return DWB_ERR_BAD_SHAPE;
-  const __half2* xp = static_cast<const __half2*>(x);
-  const __half2* dyp = static_cast<const __half2*>(dy);
-  int Bi = static_cast<int>(B), Hi = static_cast<int>(H), Wi = static_cast<int>(W), Ci = static_cast<int>(C);
-  long long rpc = rows_per_chunk, nch = nchunks_used;
-  void* args[9] = {&xp, &dyp, &dw, &Bi, &Hi, &Wi, &Ci, &rpc, &nch};
-  const cudaError_t e = launch_kernel(wgrad_for(K),
-                                      dim3(static_cast<unsigned>(cblocks), K * wgrad_nkw(K), static_cast<unsigned>(zblocks)),
-                                      dim3(kWgradWarps * 32), args, 0, static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) {
-    (void)cudaGetLastError();
-    return DWB_ERR_CUDA;
-  }
-  return DWB_OK;
-}
 
 extern "C" int dwb_weight_rot180(const void* w, void* w_rot180, int64_t C, int K, void* stream) {
   using namespace dwb;

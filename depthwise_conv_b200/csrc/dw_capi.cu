@@ -7,6 +7,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
@@ -15,6 +16,7 @@
 #include <tuple>
 
 #include "../../include/dwconv_b200.h"
+#include "dw_backward.h"
 #include "dw_kernel.cuh"
 #include "dw_launch.h"
 #include "dw_planner.h"
@@ -541,6 +543,76 @@ int dwb_conv2d_nhwc_bwd_data(const void* dy, const void* w_rot180, void* dx, int
   // rotated by 180 degrees, so the forward kernel computes the input gradient.
   return launch_forward(dy, w_rot180, nullptr, nullptr, nullptr, nullptr, dx, B, H, W, C, K, DWB_ACT_NONE,
                         DWB_ACCUM_DEFAULT, stream);
+}
+
+int dwb_conv2d_nhwc_bwd_weight(const void* x, const void* dy, float* dw, int64_t B, int64_t H, int64_t W,
+                               int64_t C, int K, void* stream) {
+  if (B < 0 || H < 1 || W < 1 || C < 8 || (C % 8) != 0 || K < 1 || K > 31 || (K % 2) == 0)
+    return DWB_ERR_BAD_SHAPE;
+  if (H > (1 << 30) || W > (1 << 30) || C > (1 << 30) || B > (1 << 30)) return DWB_ERR_BAD_SHAPE;
+  if (B == 0) return DWB_OK;
+  if (!x || !dy || !dw) return DWB_ERR_NULL_POINTER;
+  if (!aligned(x, 16) || !aligned(dy, 16) || !aligned(dw, 8)) return DWB_ERR_BAD_ALIGN;
+  DeviceState* st = nullptr;
+  int rc = get_device_state(&st);
+  if (rc != DWB_OK) return rc;
+  const void* fn = wgrad_kernel_for(K);
+  if (!fn) return DWB_ERR_UNSUPPORTED;
+
+  // CTA = (64 channels, kernel row, column tile, chunk of rows); up to 4 consumer warps of 16
+  // columns; chunks sized for ~4 CTAs per SM.
+  const int ncw = static_cast<int>(std::min<long long>(4, (W + kWgradColumnsPerWarp - 1) / kWgradColumnsPerWarp));
+  const int tile_w = ncw * kWgradColumnsPerWarp;
+  const long long col_tiles = (W + tile_w - 1) / tile_w;
+  const long long cblocks = (C + kChannelsPerCta - 1) / kChannelsPerCta;
+  const long long rows = B * H;
+  const long long base = cblocks * K * col_tiles;
+  long long chunks = (4LL * st->hw.sm_count + base - 1) / base;
+  chunks = std::max<long long>(1, std::min(chunks, rows));
+  const long long rows_per_chunk = (rows + chunks - 1) / chunks;
+  chunks = (rows + rows_per_chunk - 1) / rows_per_chunk;
+  if (cblocks > 0x7fffffffLL || col_tiles * chunks > 65535) return DWB_ERR_BAD_SHAPE;
+
+  WgradParams p;
+  p.dw = dw;
+  p.B = static_cast<int>(B);
+  p.H = static_cast<int>(H);
+  p.W = static_cast<int>(W);
+  p.C = static_cast<int>(C);
+  p.tile_w = tile_w;
+  p.col_tiles = static_cast<int>(col_tiles);
+  p.rows_per_chunk = rows_per_chunk;
+  p.consumer_warps = ncw;
+  p.stages = 4;
+  p.ring_off = kBarrierBytes;
+  p.stage_bytes = static_cast<uint32_t>(2 * tile_w + K - 1) * kPixelBytes;
+  p.err = st->err_word;
+  const int smem = static_cast<int>(p.ring_off + p.stages * p.stage_bytes);
+  {
+    static int smem_set[kMaxDevices][32];  // largest dynamic smem allowed so far, per device and K
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(st->mu);
+    if (smem_set[dev][K] < smem) {
+      const cudaError_t ce = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (ce != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(dw_wgrad_kernel)", ce);
+      smem_set[dev][K] = smem;
+    }
+  }
+  CUtensorMap tmx, tmdy;
+  rc = encode_x_map(&tmx, x, B, H, W, C, tile_w + K - 1);
+  if (rc != DWB_OK) return rc;
+  rc = encode_x_map(&tmdy, dy, B, H, W, C, tile_w);
+  if (rc != DWB_OK) return rc;
+  void* args[3] = {&tmx, &tmdy, &p};
+  const cudaError_t ce = launch_kernel(fn, dim3(static_cast<unsigned>(cblocks), K, static_cast<unsigned>(col_tiles * chunks)),
+                                       dim3(32 * (ncw + 1)), args, static_cast<size_t>(smem),
+                                       static_cast<cudaStream_t>(stream));
+  if (ce != cudaSuccess) {
+    (void)cudaGetLastError();
+    return cuda_fail("cudaLaunchKernelExC(dw_wgrad_kernel)", ce);
+  }
+  return DWB_OK;
 }
 
 int dwb_conv2d_nhwc_fused_fwd(const void* x, const void* w, const void* bias, const void* scale, const void* shift,
