@@ -199,6 +199,35 @@ def cpu_convmixer_rate(seconds: float, max_images: int | None = None):
     return n / el, threads, n, el
 
 
+def cpu_layer_us(B, H, W, C, K, seconds: float = 5.0):
+    """The reference's CPU path for one depthwise layer -- torch fp32 conv2d(groups=C), NCHW and
+    channels_last, the faster kept -- timed on this host's cores on a bounded sample of images
+    and scaled to the whole batch: (µs per layer of B images, threads, images timed, layout)."""
+    import torch
+    import torch.nn.functional as F
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(1, C, H, W, generator=g)
+    w = torch.randn(C, 1, K, K, generator=g) / K
+    best = None
+    for layout in ("nchw", "channels_last"):
+        xi = x.contiguous(memory_format=torch.channels_last) if layout == "channels_last" else x
+        F.conv2d(xi, w, padding=K // 2, groups=C)  # warm-up
+        n, t0 = 0, time.perf_counter()
+        while True:
+            F.conv2d(xi, w, padding=K // 2, groups=C)
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= seconds / 2 or n >= 10000:
+                break
+        per_image = el / n
+        if best is None or per_image < best[0]:
+            best = (per_image, n, layout)
+    return best[0] * B * 1e6, threads, best[1], best[2]
+
+
 # ----------------------------------------------------------------------------- our arm
 
 def run_ours(args):
@@ -524,6 +553,11 @@ def run_dw(args):
         "gpu_launches": args.steps,  # the timed (cold) loop; the warm graph is timed separately
         "clocks": clk,
     }
+    if world == 1 and not args.no_cpu_baseline:
+        cpu_us, threads, n, layout = cpu_layer_us(Bg, H, W, C, K)
+        line["cpu_baseline"] = {"value": cpu_us, "unit": "us/layer", "cores": threads, "kind": "reference",
+                                "sample": f"{n} single-image fp32 conv2d(groups=C) calls ({layout}) on the host, "
+                                          f"scaled to B={Bg}; epilogue not included"}
     print(json.dumps(line), flush=True)
 
 
