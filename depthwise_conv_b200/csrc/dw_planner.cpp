@@ -1,16 +1,22 @@
-// dw_planner.cpp -- choose (R, M, tile, rings) for the row-streaming kernel.
+// dw_planner.cpp -- choose (R, M, tile, row split, stage ring depth, load
+// schedule) for the row-streaming kernel.
 //
 // The planner enumerates the compiled variants and tile shapes and keeps the
 // one with the lowest modelled time on the busiest SM:
 //   * work is counted in FMA-pipe clocks per warp: a valid (output row,
-//     kernel row) pair costs 2*R*K clocks of FFMA2 plus the conversion of the
-//     R + K - 1 staged inputs, and every kernel row costs the conversion of
-//     its K weights; rows whose input falls outside the image are not counted
-//     (the kernel skips them);
+//     kernel row) pair costs 2*R*K clocks plus the flush (mixed) or the
+//     conversion of the R + K - 1 staged inputs (fp32), and every kernel row
+//     costs its K weights; rows whose input falls outside the image are not
+//     counted (the kernel skips them);
 //   * an SM runs min(ctas_per_sm, ...) CTAs at once over 4 sub-partitions;
 //     fewer than one resident warp per sub-partition idles the others;
-//   * every CTA streams (rows + weight rows) x 128-byte pixels from L2, at
-//     about 64 bytes per clock per SM.
+//   * every CTA streams its stages (input row + weight row) of 128-byte
+//     pixels from L2, at about 64 bytes per clock per SM, and pays the load
+//     latency once per step it cannot prefetch (ring depth);
+//   * a row split S divides a slot's kernel rows over S warps (one warp's
+//     critical path shrinks, the partial sums are handed over at the end);
+//   * the load schedule is the one measured better for the kernel size
+//     (default_load_schedule); the tuner measures both.
 #include "dw_planner.h"
 
 #include <algorithm>
