@@ -599,7 +599,7 @@ def run_reference(args):
 def main():
     args = parse_args()
     if args.impl == "reference":
-        args.warmup = min(args.warmup, 2)  # each CPU step is one image (~0.1 s on the GPU hosts)
+        args.warmup = max(args.warmup, 3)  # at least 3 untimed steps, as for the GPU arm
         run_reference(args)
     elif args.workload == "dw":
         run_dw(args)

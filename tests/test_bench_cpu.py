@@ -52,3 +52,15 @@ def test_cli_surface():
                          check=True).stdout
     for flag in ("--gpus", "--steps", "--warmup", "--impl", "--workload", "--shape", "--epilogue", "--backward"):
         assert flag in out
+
+
+def test_reference_arm_line():
+    """The reference arm runs the CPU model and prints one contract line (at least 3 warm-up steps)."""
+    import json
+    res = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
+                          "--warmup", "1"], capture_output=True, text=True, check=True, timeout=600)
+    line = json.loads(res.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["unit"] == "img/s" and line["higher_is_better"] is True
+    assert line["warmup"] >= 3 and line["steps"] == 1 and line["value"] > 0
+    assert line["cpu_baseline"]["value"] == line["value"] and line["cpu_baseline"]["cores"] >= 1
+    assert line["e2e"] == {"value": line["value"], "unit": "img/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
