@@ -12,7 +12,8 @@ running var 1.
 ``depthwise::conv2d_nhwc_fused`` call that computes
 ``act(conv(x) + b) * s + t + x`` in a single kernel, with s, t the
 inference-mode BN fold (benchmark_cudnn_fused_e2e.py:115-134, :125-131), and
-each 1x1 conv -> act -> BN for a GEMM plus one fused elementwise kernel.
+each 1x1 conv -> act -> BN (and the patch-conv stem) for a GEMM plus one
+fused elementwise kernel.
 """
 from __future__ import annotations
 
@@ -148,8 +149,33 @@ class FusedPointwiseBlock(nn.Module):
         return _epilogue(z, self.bias, self.scale, self.shift, self.act)
 
 
+def patch_matrix(x: torch.Tensor, p: int, k_pad: int) -> torch.Tensor:
+    """The non-overlapping p x p patches of an image batch as a [B*Ho*Wo, k_pad] row-major matrix.
+
+    Row (b, ho, wo) holds the patch's taps in (kh, kw, c_in) order, so a patch
+    convolution (stride = kernel, no padding) is this matrix times its weight
+    arranged [kh, kw, c_in] x C_out, and the product is already NHWC.  Columns
+    past p*p*C_in are zero (rows padded to a multiple of 8 halves keep the GEMM's
+    operand rows 16-byte aligned).  One copy for the rearrangement plus one fill.
+    """
+    B, Cin, H, W = x.shape
+    Ho, Wo = H // p, W // p
+    K = p * p * Cin
+    xs = x[:, :, :Ho * p, :Wo * p].permute(0, 2, 3, 1).reshape(B, Ho, p, Wo, p, Cin)  # NHWC patches
+    a = x.new_zeros(B * Ho * Wo, k_pad) if k_pad > K else x.new_empty(B * Ho * Wo, K)
+    a[:, :K].view(B, Ho, Wo, p, p, Cin).copy_(xs.permute(0, 1, 3, 2, 4, 5))
+    return a
+
+
 class FusedStem(nn.Module):
-    """Patch conv -> act -> BN: cuDNN convolution without bias, then one elementwise pass."""
+    """Patch conv -> act -> BN.
+
+    With stride = kernel and no padding (every ConvMixer stem) the patches do
+    not overlap and the convolution is one GEMM: ``patch_matrix`` times the
+    [p*p*C_in, C] weight (cuBLAS), whose output is the NHWC activation, then one
+    elementwise pass for the bias, the activation and the BN fold.  Any other
+    stem runs cuDNN's convolution before the same elementwise pass.
+    """
 
     def __init__(self, conv: nn.Conv2d, act: str, bn: nn.BatchNorm2d):
         super().__init__()
@@ -164,11 +190,27 @@ class FusedStem(nn.Module):
         self.register_buffer("shift", shift.half().contiguous())
         self.stride = conv.stride
         self.act = act
+        kh, kw = conv.kernel_size
+        self.patch = kh if (kh == kw and conv.stride == (kh, kw) and conv.groups == 1 and conv.dilation == (1, 1)
+                            and conv.padding in ((0, 0), "valid")) else 0
+        if self.patch:
+            K = kh * kw * conv.in_channels
+            self.k_pad = (K + 7) // 8 * 8
+            with torch.no_grad():
+                wt = torch.zeros(self.k_pad, C, dtype=torch.float16, device=conv.weight.device)
+                wt[:K] = conv.weight.detach().permute(2, 3, 1, 0).reshape(K, C).half()  # [kh, kw, c_in] x C
+            self.register_buffer("weight_t", wt)
 
     def forward(self, x):
-        z = torch.nn.functional.conv2d(x, self.weight, None, self.stride)
-        if not z.is_contiguous(memory_format=torch.channels_last):
-            z = z.contiguous(memory_format=torch.channels_last)
+        if self.patch:
+            B, _, H, W = x.shape
+            Ho, Wo = H // self.patch, W // self.patch
+            z = torch.mm(patch_matrix(x, self.patch, self.k_pad), self.weight_t)  # [B*Ho*Wo, C], NHWC
+            z = z.view(B, Ho, Wo, -1).permute(0, 3, 1, 2)  # channels_last view
+        else:
+            z = torch.nn.functional.conv2d(x, self.weight, None, self.stride)
+            if not z.is_contiguous(memory_format=torch.channels_last):
+                z = z.contiguous(memory_format=torch.channels_last)
         return _epilogue(z, self.bias, self.scale, self.shift, self.act)
 
 

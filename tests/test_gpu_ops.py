@@ -255,6 +255,39 @@ def test_bias_act_affine(eng, act):
     assert torch.equal(xd, y)
 
 
+@pytest.mark.parametrize("B,H,W,C,offset,with_scale", [(4, 32, 32, 1536, 0, True), (4, 64, 64, 200, 0, False),
+                                                        (4, 64, 64, 200, 2, True), (1, 3, 5, 24, 2, False)])
+def test_bias_act_affine_strides_and_parameter_alignment(eng, B, H, W, C, offset, with_scale):
+    """More 8-channel groups than the grid has threads (the channel index advances across grid
+    strides), channel counts that do not divide the grid, parameter vectors only 4-byte aligned
+    (offset halves into their allocation), and an absent scale."""
+    from math import sqrt
+
+    from scipy.special import erf
+    rng = np.random.default_rng(B * 1000 + C + offset)
+    x = (rng.standard_normal((B, H, W, C)) * 2).astype(np.float16)
+    b = (rng.standard_normal(C) * 0.5).astype(np.float16)
+    s = rng.uniform(0.5, 1.5, C).astype(np.float16)
+    t = (rng.standard_normal(C) * 0.5).astype(np.float16)
+    v = x.astype(np.float64) + b.astype(np.float64)
+    gs = 0.5 * v * (1 + erf(v / sqrt(2))) * (s.astype(np.float64) if with_scale else 1.0)
+    exact = gs + t.astype(np.float64)
+
+    def vec(a):
+        buf = torch.zeros(C + offset, dtype=torch.float16, device="cuda")
+        buf[offset:] = torch.from_numpy(a).cuda()
+        return buf[offset:]
+
+    y = eng.dw_ops.bias_act_affine(to_dev(x), vec(b), vec(s) if with_scale else None, vec(t), "gelu")
+    torch.cuda.synchronize()
+    got = to_host(y).astype(np.float64)
+    ulp = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(exact), 2.0 ** -14))) - 10)
+    # 2 ulp of the result, plus 1e-4 of the GELU term: where act(v) * s nearly cancels t, the erfc
+    # approximation's tail error (about 4e-5 of the term near v = -2.9, well inside one fp16 ulp of
+    # the term) outgrows the ulp of the small result
+    assert (np.abs(got - exact) <= 2 * ulp + 1e-7 + 1e-4 * np.abs(gs)).all()
+
+
 def test_probe_fma_peak_reports_plausible_rates(eng):
     h, f = eng.probe_fma_peak()
     assert 10.0 < h < 200.0 and 10.0 < f < 200.0

@@ -161,3 +161,30 @@ def test_convmixer_models_share_weights_with_cpu_reference():
     x = torch.randn(1, 3, 28, 28)
     with torch.no_grad():
         np.testing.assert_allclose(gpu_model(x).numpy(), cpu_model(x).numpy(), rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("B,Cin,H,W,p,C,channels_last", [(2, 3, 224, 224, 7, 64, True), (1, 3, 30, 29, 7, 16, True),
+                                                         (2, 3, 28, 28, 14, 8, False), (1, 5, 9, 9, 3, 12, False)])
+def test_stem_patch_gemm_equals_patch_conv(eng, B, Cin, H, W, p, C, channels_last):
+    """The ConvMixer stem's GEMM form (patch matrix x [kh, kw, c_in] x C weight, rows zero-padded to a
+    multiple of 8) equals the strided patch convolution, including sizes that do not divide by p."""
+    from depthwise_conv_b200.convmixer import FusedStem, patch_matrix
+    torch.manual_seed(p * 100 + C)
+    conv = nn.Conv2d(Cin, C, p, stride=p)
+    stem = FusedStem(conv, "gelu", nn.BatchNorm2d(C).eval())
+    K = p * p * Cin
+    assert stem.patch == p and stem.k_pad % 8 == 0 and stem.k_pad - K < 8
+    x = torch.randn(B, Cin, H, W)
+    if channels_last:
+        x = x.contiguous(memory_format=torch.channels_last)
+    a = patch_matrix(x, p, stem.k_pad)
+    assert a.shape == (B * (H // p) * (W // p), stem.k_pad) and (a[:, K:] == 0).all()
+    z = (a @ stem.weight_t.float()).view(B, H // p, W // p, C).permute(0, 3, 1, 2)
+    ref = torch.nn.functional.conv2d(x, conv.weight.detach().half().float(), None, p)
+    assert torch.allclose(z, ref, atol=1e-4, rtol=1e-4)
+
+
+def test_stem_keeps_the_convolution_for_overlapping_patches(eng):
+    from depthwise_conv_b200.convmixer import FusedStem
+    assert FusedStem(nn.Conv2d(3, 16, 7, stride=4), "gelu", nn.BatchNorm2d(16).eval()).patch == 0
+    assert FusedStem(nn.Conv2d(3, 16, 7, stride=7, padding=1), "gelu", nn.BatchNorm2d(16).eval()).patch == 0
