@@ -146,6 +146,54 @@ def call(fn: str, *args) -> None:
     check(fn, getattr(load(), fn)(*args))
 
 
+# Opt-in check of the device error word after every engine launch made through the torch ops.
+# A kernel whose bounded wait expires (its data never arrived within ~1 s of SM clock) records a
+# code in the word and returns with its output partly unwritten; without this check only an
+# explicit device_error() call reveals it.  The check synchronises the launching stream, so it is
+# for debugging and validation runs, and it is skipped while the stream is being captured into a
+# CUDA graph (no synchronisation is allowed there).  Enabled by DWB_CHECK_DEVICE_ERROR=1 in the
+# environment, or set_check_device_error(True).
+_check_device_error = os.environ.get("DWB_CHECK_DEVICE_ERROR", "0") not in ("", "0")
+
+
+def set_check_device_error(on: bool) -> bool:
+    """Turn the post-launch device-error check on or off; returns the previous setting."""
+    global _check_device_error
+    prev, _check_device_error = _check_device_error, bool(on)
+    return prev
+
+
+def check_device_error_enabled() -> bool:
+    return _check_device_error
+
+
+class DeviceTimeoutError(RuntimeError):
+    """A kernel's bounded wait expired: its output is incomplete (device error word set)."""
+
+    def __init__(self, code: int, where: str):
+        self.code = code
+        super().__init__(f"{where}: a kernel's bounded wait expired (device error code {code}: "
+                         f"{DEVICE_ERROR_CODES.get(code, 'unknown')}); its output is incomplete")
+
+
+# Codes a kernel stores in the device error word (csrc/dw_device.cuh).
+DEVICE_ERROR_CODES = {1: "stage wait before a tile's first step", 2: "stage wait of a step",
+                      3: "producer's free-stage wait", 4: "row-split partial-sum hand-off",
+                      5: "bounded-wait self-test"}
+
+
+def after_launch(stream: int, where: str) -> None:
+    """The opt-in post-launch check: raise DeviceTimeoutError if the device error word is set."""
+    if not _check_device_error:
+        return
+    import torch
+    if torch.cuda.is_current_stream_capturing():
+        return
+    code = device_error(stream, clear=True)
+    if code:
+        raise DeviceTimeoutError(code, where)
+
+
 def plan_query(B: int, H: int, W: int, C: int, K: int, accum: int = ACCUM_DEFAULT, sm_count: int = 0,
                smem_optin: int = 0) -> dict:
     """The planner's choice for a problem (host arithmetic only, no GPU needed)."""

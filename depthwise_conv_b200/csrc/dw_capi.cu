@@ -734,11 +734,28 @@ int dwb_device_error(int* code_out, int clear, void* stream) {
 // share the one buffer: each call overwrites the K*K*C entries it uses before
 // reading them (nothing needs to start at zero), and calls on one device whose
 // work overlaps on the GPU (for example on two streams) race on it: order them.
+// Only a successful lookup is remembered: a lookup that failed (for example one
+// attempted during a stream capture) is tried again by the next call.
 constexpr long long kNoAllocMaxTaps = 1LL << 21;  // K*K*C fp16 taps
 static __device__ __align__(256) __half g_noalloc_rot_taps[kNoAllocMaxTaps];
-static std::once_flag g_noalloc_once[kMaxDevices];
+static std::mutex g_noalloc_mu[kMaxDevices];
 static void* g_noalloc_taps[kMaxDevices];
-static cudaError_t g_noalloc_lookup[kMaxDevices];
+
+// Device address of the built-in buffer on device `dev` (current), looked up once.
+static int noalloc_taps(int dev, void** out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu[dev]);
+  if (!g_noalloc_taps[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_rot_taps);
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();
+      return cuda_fail("cudaGetSymbolAddress(g_noalloc_rot_taps)", e);
+    }
+    g_noalloc_taps[dev] = p;
+  }
+  *out = g_noalloc_taps[dev];
+  return DWB_OK;
+}
 
 int dwb_conv2d_nhwc_bwd_data_noalloc(const void* dy, const void* w, void* dx, int64_t B, int64_t H, int64_t W,
                                      int64_t C, int K, void* stream) {
@@ -754,13 +771,12 @@ int dwb_conv2d_nhwc_bwd_data_noalloc(const void* dy, const void* w, void* dx, in
   if (B == 0) return DWB_OK;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return DWB_ERR_NO_DEVICE;
-  std::call_once(g_noalloc_once[dev], [dev] {
-    g_noalloc_lookup[dev] = cudaGetSymbolAddress(&g_noalloc_taps[dev], g_noalloc_rot_taps);
-  });
-  if (g_noalloc_lookup[dev] != cudaSuccess) return cuda_fail("cudaGetSymbolAddress(g_noalloc_rot_taps)", g_noalloc_lookup[dev]);
-  rc = dwb_weight_rot180(w, g_noalloc_taps[dev], C, K, stream);
+  void* taps = nullptr;
+  rc = noalloc_taps(dev, &taps);
   if (rc != DWB_OK) return rc;
-  return launch_forward(dy, g_noalloc_taps[dev], nullptr, nullptr, nullptr, nullptr, dx, B, H, W, C, K, DWB_ACT_NONE,
+  rc = dwb_weight_rot180(w, taps, C, K, stream);
+  if (rc != DWB_OK) return rc;
+  return launch_forward(dy, taps, nullptr, nullptr, nullptr, nullptr, dx, B, H, W, C, K, DWB_ACT_NONE,
                         DWB_ACCUM_DEFAULT, stream);
 }
 

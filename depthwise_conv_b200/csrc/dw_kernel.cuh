@@ -243,7 +243,9 @@ constexpr RegCap kRegCaps[] = {
     {0, 0, 0, 0, 0, 255}};
 template <int K, int R, int M, int ACC, int PRE>
 constexpr int reg_cap() {
-#ifdef DWB_NO_REGCAPS
+#if defined(DWB_FORCE_CAP)
+  return DWB_FORCE_CAP;  // build.py --regcaps: every variant at one cap, to read ptxas's spills
+#elif defined(DWB_NO_REGCAPS)
   return 255;
 #else
   for (const RegCap& c : kRegCaps)

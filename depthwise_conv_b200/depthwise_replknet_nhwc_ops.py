@@ -51,6 +51,7 @@ def _replknet_op(fn: str, input, weight, bias, C: int, HW: int, K: int):
             _lib.call("dwb_conv2d_nhwc_fused_fwd", input.data_ptr(), weight.data_ptr(), bp or None, None, None,
                       None, output.data_ptr(), B, Hi, Wi, Ci, K, _lib.ACT_NONE, _lib.ACCUM_DEFAULT,
                       torch.cuda.current_stream(input.device).cuda_stream)
+        _lib.after_launch(torch.cuda.current_stream(input.device).cuda_stream, fn or "dwb_conv2d_nhwc_fused_fwd")
     return output
 
 

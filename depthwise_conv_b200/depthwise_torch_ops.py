@@ -58,6 +58,7 @@ def _fixed_op(fn: str, input: torch.Tensor, weight: torch.Tensor, H: int, W: int
     args.append(_stream(input))
     with dw_ops._DeviceGuard(input.device):
         _lib.call(fn, *args)
+        _lib.after_launch(_stream(input), fn)
     return output
 
 

@@ -15,10 +15,13 @@ Generic ops (new; the reference only has fixed-shape ops):
   (benchmark_cudnn_fused_e2e.py:44-84,115-134) plus ConvMixer's residual
   (convmixer/convmixer.py:58-59).
 
-``depthwise::conv2d_nhwc`` is differentiable (``torch.library.register_autograd``):
-the input gradient runs the forward kernel on dy with the taps rotated by 180
-degrees, the weight gradient a dedicated kernel accumulating in fp32, the bias
-gradient a channel sum.  The reference's ops are inference-only.
+``depthwise::conv2d_nhwc`` and ``depthwise::conv2d_nhwc_fused`` are
+differentiable (``torch.library.register_autograd``): the input gradient runs
+the forward kernel on dy with the taps rotated by 180 degrees, the weight
+gradient a dedicated kernel accumulating in fp32, the bias gradient a channel
+sum; the fused op recomputes its pre-activation with the engine and takes the
+elementwise adjoints (activation, BN scale/shift, residual) in fp32.  The
+reference's ops are inference-only.
 """
 from __future__ import annotations
 
@@ -122,6 +125,7 @@ def conv2d_nhwc_fused(x: torch.Tensor, w: torch.Tensor, bias=None, scale=None, s
             _lib.call("dwb_conv2d_nhwc_fwd_planned", x.data_ptr(), w.data_ptr(), bp or None, sp or None,
                       hp or None, rp or None, y.data_ptr(), B, H, W, C, K, act_code, ctypes.byref(pl),
                       _stream_of(x))
+        _lib.after_launch(_stream_of(x), "depthwise conv2d_nhwc_fused")
     return y
 
 
@@ -140,6 +144,7 @@ def bias_act_affine(x: torch.Tensor, bias=None, scale=None, shift=None, act: int
     with _DeviceGuard(x.device):
         _lib.call("dwb_bias_act_affine_nhwc", x.data_ptr(), bp or None, sp or None, hp or None, y.data_ptr(),
                   B * H * W, C, act_code, _stream_of(x))
+        _lib.after_launch(_stream_of(x), "depthwise bias_act_affine")
     return y
 
 
@@ -163,6 +168,7 @@ def conv2d_nhwc_backward_input(dy: torch.Tensor, w: torch.Tensor) -> torch.Tenso
     with _DeviceGuard(dy.device):
         _lib.call("dwb_conv2d_nhwc_bwd_data", dy.data_ptr(), wr.data_ptr(), dx.data_ptr(), B, H, W, C, K,
                   _stream_of(dy))
+        _lib.after_launch(_stream_of(dy), "depthwise conv2d_nhwc input gradient")
     return dx
 
 
@@ -177,6 +183,7 @@ def conv2d_nhwc_backward_weight(x: torch.Tensor, dy: torch.Tensor, K: int) -> to
     with _DeviceGuard(x.device):
         _lib.call("dwb_conv2d_nhwc_bwd_weight", x.data_ptr(), dy.data_ptr(), dw.data_ptr(), B, H, W, C, K,
                   _stream_of(x))
+        _lib.after_launch(_stream_of(x), "depthwise conv2d_nhwc weight gradient")
     return dw
 
 
@@ -245,3 +252,55 @@ def _conv2d_nhwc_backward(ctx, grad):
 
 
 torch.library.register_autograd("depthwise::conv2d_nhwc", _conv2d_nhwc_backward, setup_context=_conv2d_nhwc_setup)
+
+
+# Backward of the fused op y = act(z) * scale + shift + residual, z = conv(x, w) + bias.  The
+# forward keeps nothing but its inputs; the backward recomputes z with the engine (one launch), takes
+# the elementwise adjoints in fp32 with PyTorch, and runs the engine's two gradient kernels on
+#   gz = dy * scale * act'(z):   dx = conv_input_grad(gz) (+ dy through the residual),
+#   dw = conv_weight_grad(x, gz), dbias = sum gz, dscale = sum dy * act(z), dshift = sum dy.
+# act'(z): ReLU 1[z > 0]; GELU (exact form) Phi(z) + z * phi(z).
+
+def _conv2d_nhwc_fused_setup(ctx, inputs, output):
+    x, w, bias, scale, shift, residual, act = inputs
+    ctx.save_for_backward(x, w, bias, scale)
+    ctx.act = int(act)
+    ctx.flags = (bias is not None, scale is not None, shift is not None, residual is not None)
+
+
+def _conv2d_nhwc_fused_backward(ctx, grad):
+    x, w, bias, scale = ctx.saved_tensors
+    has_bias, has_scale, has_shift, has_res = ctx.flags
+    g = grad if grad.is_contiguous(memory_format=torch.channels_last) else grad.contiguous(
+        memory_format=torch.channels_last)
+    gf = g.float()
+    need = ctx.needs_input_grad
+    dims = (0, 2, 3)
+    gz = gf
+    a = None
+    if ctx.act != _lib.ACT_NONE or (has_scale and need[3]):
+        z = conv2d_nhwc_fused(x, w, bias=bias).float()
+        if ctx.act == _lib.ACT_RELU:
+            a = torch.relu(z)
+            gz = gz * (z > 0).to(gz.dtype)
+        elif ctx.act == _lib.ACT_GELU:
+            cdf = 0.5 * (1.0 + torch.erf(z * 0.7071067811865476))
+            pdf = torch.exp(-0.5 * z * z) * 0.3989422804014327
+            a = z * cdf
+            gz = gz * (cdf + z * pdf)
+        else:
+            a = z
+    if has_scale:
+        gz = gz * scale.float().view(1, -1, 1, 1)
+    gz16 = gz.to(x.dtype).contiguous(memory_format=torch.channels_last)
+    dx = conv2d_nhwc_backward_input(gz16, w) if need[0] else None
+    dw = conv2d_nhwc_backward_weight(x, gz16, w.shape[0]).to(w.dtype) if need[1] else None
+    db = gz.sum(dim=dims).to(x.dtype) if has_bias and need[2] else None
+    ds = (gf * a).sum(dim=dims).to(x.dtype) if has_scale and need[3] else None
+    dt = gf.sum(dim=dims).to(x.dtype) if has_shift and need[4] else None
+    dr = g if has_res and need[5] else None
+    return dx, dw, db, ds, dt, dr, None
+
+
+torch.library.register_autograd("depthwise::conv2d_nhwc_fused", _conv2d_nhwc_fused_backward,
+                                setup_context=_conv2d_nhwc_fused_setup)

@@ -242,7 +242,8 @@ DWB_API int dwb_conv2d_nhwc_bwd_weight(const void* x, const void* dy, float* dw,
  * library (every GPU that loads the library holds it until exit), so K*K*C
  * must be at most 2097152 (DWB_ERR_BAD_SHAPE and a dwb_last_error message
  * otherwise).  The first call on a device looks up the buffer's address
- * (cudaGetSymbolAddress): make that first call before any stream capture.
+ * (cudaGetSymbolAddress): make that first call before any stream capture
+ * (a lookup that fails is not remembered; the next call tries again).
  * All calls share the buffer: calls on one device whose work overlaps on the
  * GPU race on it. */
 DWB_API int dwb_conv2d_nhwc_bwd_data_noalloc(const void* dy, const void* w, void* dx, int64_t B, int64_t H,

@@ -64,3 +64,21 @@ def test_reference_arm_line():
     assert line["warmup"] >= 3 and line["steps"] == 1 and line["value"] > 0
     assert line["cpu_baseline"]["value"] == line["value"] and line["cpu_baseline"]["cores"] >= 1
     assert line["e2e"] == {"value": line["value"], "unit": "img/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_dw_configs_cover_every_baseline_layer():
+    """18 layer entries: RepLKNet C3-C6 and the ConvMixer layers C1/C2 at B=1, the k9 batch sweep at
+    B in {1, 16, 64, 256} and the k-sweep at B=64 with GELU+BN (BASELINE configs[1..4])."""
+    names = [c[0] for c in bench.DW_CONFIGS]
+    assert len(names) == len(set(names)) == 18
+    shapes = {(B, H, W, C, K, epi) for _, B, H, W, C, K, epi, _ in bench.DW_CONFIGS}
+    for s in [(1, 32, 32, 768, 7, "none"), (1, 32, 32, 1536, 9, "none"), (1, 56, 56, 128, 31, "none"),
+              (1, 28, 28, 256, 29, "none"), (1, 14, 14, 512, 27, "none"), (1, 7, 7, 1024, 13, "none")]:
+        assert s in shapes
+    for b in (1, 16, 64, 256):
+        assert (b, 32, 32, 1536, 9, "none") in shapes
+    for k in (7, 9, 13, 17, 21, 27, 29, 31):
+        assert (64, 56, 56, 1024, k, "gelu_bn") in shapes
+    # batched configs shard over the ranks; batch-1 configs are per-GPU replicas
+    for _, B, *_rest, shard in bench.DW_CONFIGS:
+        assert shard == ("replica" if B == 1 else "batch")

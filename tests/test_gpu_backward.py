@@ -34,8 +34,11 @@ def to_host(t):
     return t.permute(0, 2, 3, 1).contiguous().cpu().numpy() if t.dim() == 4 else t.cpu().numpy()
 
 
+# The last two need more than one weight-gradient column tile (W > 64, W not a multiple of 64: the
+# right-edge zero fill and the column-tile offsets of the loads); in (2, 5, 130, 72, 31) the B*H = 10
+# rows split into chunks of 3, so one row chunk spans two images.
 SHAPES = [(2, 19, 21, 72, 7), (1, 9, 30, 64, 31), (3, 5, 11, 64, 9), (1, 14, 14, 512, 27), (2, 1, 1, 8, 1),
-          (2, 23, 17, 136, 13), (1, 3, 40, 16, 29)]
+          (2, 23, 17, 136, 13), (1, 3, 40, 16, 29), (1, 6, 100, 64, 7), (2, 5, 130, 72, 31)]
 
 
 def _problem(B, H, W, C, K):
@@ -104,4 +107,37 @@ def test_autograd_through_the_op(eng, oracle_mod, with_bias):
     if with_bias:
         gb = bt.grad.cpu().numpy().astype(np.float64)
         assert np.abs(gb - db_exact).max() <= 1e-3 * np.abs(db_exact).max() + 1e-3
+    assert eng.device_error() == 0
+
+
+@pytest.mark.parametrize("act", ["none", "relu", "gelu"])
+def test_autograd_through_the_fused_op(eng, act):
+    """loss = sum(conv2d_nhwc_fused(x, w, b, s, t, x, act) * g): every gradient against float64 torch
+    autograd of the same composition (F.conv2d groups=C, activation, scale/shift, residual)."""
+    import torch.nn.functional as F
+    B, H, W, C, K = 2, 12, 14, 64, 7
+    x, w, dy = _problem(B, H, W, C, K)
+    rng = np.random.default_rng(11)
+    b = (rng.standard_normal(C) * 0.1).astype(np.float16)
+    s = rng.uniform(0.5, 1.5, C).astype(np.float16)
+    t = (rng.standard_normal(C) * 0.1).astype(np.float16)
+    code = {"none": 0, "relu": 1, "gelu": 2}[act]
+    leaves = [to_dev(a).requires_grad_() for a in (x, w, b, s, t)]
+    xt, wt, bt, st, tt = leaves
+    y = torch.ops.depthwise.conv2d_nhwc_fused(xt, wt, bt, st, tt, xt, code)
+    y.backward(to_dev(dy))
+    torch.cuda.synchronize()
+    # float64 reference on the CPU
+    r = [torch.from_numpy(a.astype(np.float64)).requires_grad_() for a in (x, w, b, s, t)]
+    rx, rw, rb, rs, rt = r
+    xc = rx.permute(0, 3, 1, 2)
+    z = F.conv2d(xc, rw.permute(2, 0, 1).unsqueeze(1), rb, padding=K // 2, groups=C)
+    a = {"none": z, "relu": torch.relu(z), "gelu": F.gelu(z)}[act]
+    yr = a * rs.view(1, -1, 1, 1) + rt.view(1, -1, 1, 1) + xc
+    yr.backward(torch.from_numpy(dy.astype(np.float64)).permute(0, 3, 1, 2))
+    for name, got, ref in zip("x w b s t".split(), leaves, r):
+        gv = to_host(got.grad).astype(np.float64) if got.dim() == 4 else got.grad.cpu().numpy().astype(np.float64)
+        rv = ref.grad.numpy()
+        rel = np.linalg.norm(gv - rv) / (np.linalg.norm(rv) + 1e-30)
+        assert rel < 5e-3, f"d{name}: rel-L2 {rel:.2e}"
     assert eng.device_error() == 0

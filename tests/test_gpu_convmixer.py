@@ -110,3 +110,71 @@ def test_convmixer_compiled_reduce_overhead_replay():
             outs.append(yc)
     diffs = [(outs[i] - outs[i + 1]).abs().max().item() for i in range(4)]
     assert all(d > 0 for d in diffs)
+
+
+def _signal_preserving_pair(name, seed=5):
+    """The GPU model and the fp32 CPU model with identical weights scaled so that the signal keeps an
+    O(1) size through every block: patch conv N(0, 1/(3 p^2)), DW taps N(0, 1/K^2), 1x1 convs
+    N(0, g^2/C) with g = 1.15 for GELU and 1.0 for ReLU (measured on the fp32 CPU model: feature maps
+    stay at std 0.5-4 through all blocks, logits at std 2-3), head N(0, 1/C), biases 0."""
+    import math
+
+    from depthwise_conv_b200.convmixer import convmixer
+    from oracle.convmixer_ref import convmixer_cpu
+
+    gpu = convmixer(name, seed=0)
+    cpu = convmixer_cpu(name, seed=0)
+    C, K, p, depth = cpu.dim, cpu.k, cpu.p, cpu.depth
+    gain = 1.0 if cpu.act == "relu" else 1.15
+    g = torch.Generator().manual_seed(seed)
+    cpu.patch_w = torch.randn(C, 3, p, p, generator=g) / math.sqrt(3 * p * p)
+    cpu.dw_w = [torch.randn(C, 1, K, K, generator=g) / K for _ in range(depth)]
+    cpu.pw_w = [torch.randn(C, C, 1, 1, generator=g) * gain / math.sqrt(C) for _ in range(depth)]
+    cpu.head_w = torch.randn(1000, C, generator=g) / math.sqrt(C)
+    with torch.no_grad():
+        gpu.model[0].weight.copy_(cpu.patch_w)
+        for i in range(depth):
+            blk = gpu.model[3 + i]
+            blk[0].fn[0].weight.copy_(cpu.dw_w[i])
+            blk[1].weight.copy_(cpu.pw_w[i])
+        gpu.model[-1].weight.copy_(cpu.head_w)
+    return gpu, cpu
+
+
+@pytest.mark.parametrize("name", ["1536_20", "768_32"])
+def test_convmixer_full_depth_parity(name):
+    """Every block and the logits checked: with a signal-preserving init the feature maps after the
+    middle and the last block and the logits are O(1), so the fused fp16 network is compared with the
+    fp32 CPU model at full depth (rel-L2), against the bar of PyTorch's own fp16 GPU model."""
+    from depthwise_conv_b200.convmixer import fuse_dw_blocks
+
+    gpu, cpu = _signal_preserving_pair(name)
+    base = gpu.half().cuda().to(memory_format=torch.channels_last)
+    fused = fuse_dw_blocks(copy.deepcopy(base))
+    assert fused.fused_blocks == base.depth
+    x = torch.randn(2, 3, 224, 224, generator=torch.Generator().manual_seed(9))
+    xd = x.half().cuda().contiguous(memory_format=torch.channels_last)
+    depth = base.depth
+    for n in (depth // 2, depth):
+        ref = cpu.trunk(x, blocks=n)
+        assert 0.1 < ref.std().item() < 50.0, f"signal left the O(1) range after {n} blocks"
+        with torch.no_grad():
+            t = base.model[:3 + n](xd).float().cpu()
+            f = fused.model[:3 + n](xd).float().cpu()
+        rel_t = ((t - ref).norm() / ref.norm()).item()
+        rel_f = ((f - ref).norm() / ref.norm()).item()
+        print(f"ConvMixer-{name} after {n} blocks: rel-L2 torch-fp16 {rel_t:.2e}, engine-fused {rel_f:.2e}")
+        assert rel_f <= max(1.5 * rel_t, 5e-3)
+    ref = cpu(x)
+    with torch.no_grad():
+        lt = base(xd).float().cpu()
+        lf = fused(xd).float().cpu()
+    rel_t = ((lt - ref).norm() / ref.norm()).item()
+    rel_f = ((lf - ref).norm() / ref.norm()).item()
+    print(f"ConvMixer-{name} logits (std {ref.std().item():.2f}): rel-L2 torch-fp16 {rel_t:.2e}, "
+          f"engine-fused {rel_f:.2e}")
+    assert rel_f <= max(1.5 * rel_t, 5e-3)
+    # the top classes agree wherever the fp32 margin is clear of the fp16 error
+    top2 = ref.topk(2, dim=1).values
+    clear = (top2[:, 0] - top2[:, 1]) > 0.05 * ref.std()
+    assert torch.equal(lf.argmax(1)[clear], ref.argmax(1)[clear])

@@ -313,3 +313,30 @@ def test_expired_wait_reports_and_context_survives(eng, oracle_mod):
     assert eng.device_error() == 0
     with pytest.raises(_lib.DwbError):
         _lib.selftest_bounded_wait(0)
+
+
+def test_expired_wait_raises_in_torch_path_when_checked(eng, oracle_mod):
+    """With the opt-in post-launch check on (DWB_CHECK_DEVICE_ERROR=1 or set_check_device_error), an
+    expired bounded wait surfaces as an exception from the next torch op on that device.  The expiry
+    is made without a fault: the bounded-wait self-test kernel gives up after ~1 ms and leaves code 5;
+    the op after it raises DeviceTimeoutError (a RuntimeError); the context stays usable and the op
+    then runs and matches the oracle."""
+    from depthwise_conv_b200 import _lib
+    assert eng.device_error() == 0
+    x, w = make_problem(6, 1, 16, 16, 64, 7)
+    xd, wd = to_dev(x), to_dev(w)
+    prev = _lib.set_check_device_error(True)
+    try:
+        stream = torch.cuda.current_stream().cuda_stream
+        assert _lib.load().dwb_selftest_bounded_wait(2_000_000, stream) == _lib.OK  # leaves code 5
+        with pytest.raises(RuntimeError, match="bounded wait expired"):
+            eng.conv2d_nhwc_fused(xd, wd)
+        y = eng.conv2d_nhwc_fused(xd, wd)  # the read cleared the word: this call passes the check
+        y2 = torch.ops.depthwise.conv2d_nhwc(xd, wd, None)
+    finally:
+        _lib.set_check_device_error(prev)
+    torch.cuda.synchronize()
+    exact, _ = oracle_mod.dw_forward(x, w)
+    check(oracle_mod, y, exact, "after the expired wait")
+    assert torch.equal(y, y2)
+    assert eng.device_error() == 0

@@ -15,6 +15,7 @@ the reference checkout exists).  These tests
 from __future__ import annotations
 
 import ctypes
+import json
 import os
 
 import numpy as np
@@ -111,3 +112,129 @@ def test_engine_vs_reference_kernel_and_timing(ref, oracle_mod, fn, HW, C, K):
     print(f"{fn}: ours vs exact max {e_ours[0]:.2e} rel {e_ours[1]:.2e}; reference vs exact max {e_ref[0]:.2e} "
           f"rel {e_ref[1]:.2e}; ours vs reference rel {e_between[1]:.2e}; eager us/call: reference {us_ref:.1f}, "
           f"ours {us_ours:.1f}")
+
+
+# ---- the reference's ConvMixer kernels (convmixer/kernels/depthwise_integration.cu), rebuilt for
+# sm_100a as the reference's own loader builds them (oracle/build_ref.py -> oracle/_ref/ext_convmixer/).
+# depthwise_forward_32_1536_13 calls exit(1) (depthwise_integration.cu:1013-1030): never called.
+CM_CASES = [("depthwise_forward_32_768_7", 32, 768, 7, 1), ("depthwise_forward_32_1536_9", 32, 1536, 9, 2),
+            ("depthwise_forward_32_1536_9_v2", 32, 1536, 9, 2), ("depthwise_forward_16_1536_9", 16, 1536, 9, 1)]
+
+
+@pytest.fixture(scope="module")
+def cm_ext():
+    from oracle import build_ref
+    mod = build_ref.load_ext("depthwise_convmixer")
+    if mod is None:
+        pytest.skip("reference ConvMixer extension not built (oracle/build_ref.py needs the reference checkout)")
+    return mod
+
+
+@pytest.fixture(scope="module")
+def rk_ext():
+    from oracle import build_ref
+    mod = build_ref.load_ext("depthwise_replknet_nhwc_v2")
+    if mod is None:
+        pytest.skip("reference RepLKNet extension not built (oracle/build_ref.py needs the reference checkout)")
+    return mod
+
+
+@pytest.mark.parametrize("fn,HW,C,K,B", CM_CASES, ids=[c[0] for c in CM_CASES])
+def test_reference_convmixer_kernel_matches_fp16_emulation_bitwise(cm_ext, oracle_mod, fn, HW, C, K, B):
+    """The reference's ConvMixer kernels accumulate in fp16, taps in row-major order (ki outer, kj inner,
+    depthwise_integration.cu:76-101 and :230-364); the oracle's emulation must reproduce them bit for bit."""
+    x, w = make_problem(3030 + K + HW, B, HW, HW, C, K)
+    xd = _dev(x).permute(0, 3, 1, 2)  # channels_last [B, C, H, W]
+    wd = _dev(w)
+    y = torch.empty_like(xd)
+    getattr(cm_ext, fn)(xd, wd, y, HW, HW, C, K)
+    torch.cuda.synchronize()
+    got = y.permute(0, 2, 3, 1).contiguous().cpu().numpy()
+    nimg = B if fn.startswith("depthwise_forward_32_1536_9") else 1  # the others process one image per call
+    emu = oracle_mod.dw_forward_f16acc(x[:nimg], w)
+    mism = np.count_nonzero(got[:nimg].view(np.uint16) != emu.view(np.uint16))
+    assert mism == 0, f"{mism} of {emu.size} outputs differ from the emulated reference arithmetic"
+    exact, _ = oracle_mod.dw_forward(x[:nimg], w)
+    max_err, rel = oracle_mod.parity(got[:nimg], exact)
+    print(f"{fn}: reference kernel vs exact: max {max_err:.3e} rel-L2 {rel:.3e}")
+
+
+def _graph_us(fn, reps=50):
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        fn()
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(reps):
+                fn()
+        g.replay()
+        s.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        best = 1e30
+        for _ in range(3):
+            e0.record(s)
+            g.replay()
+            e1.record(s)
+            s.synchronize()
+            best = min(best, e0.elapsed_time(e1) / reps * 1000.0)
+    return best
+
+
+def _eager_us(fn, n=200):
+    for _ in range(20):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / n * 1000.0
+
+
+TIMED = [("C1", "cm", "depthwise_forward_32_768_7", 1, 32, 768, 7),
+         ("C2", "cm", "depthwise_forward_32_1536_9", 1, 32, 1536, 9),
+         ("16x16x1536_k9", "cm", "depthwise_forward_16_1536_9", 1, 16, 1536, 9),
+         ("bsweep_k9_b16", "cm", "depthwise_forward_32_1536_9", 16, 32, 1536, 9),
+         ("bsweep_k9_b64", "cm", "depthwise_forward_32_1536_9", 64, 32, 1536, 9),
+         ("bsweep_k9_b256", "cm", "depthwise_forward_32_1536_9", 256, 32, 1536, 9),
+         ("C3", "rk", "depthwise_31x31_128_nhwc", 1, 56, 128, 31),
+         ("C4", "rk", "depthwise_29x29_256_nhwc", 1, 28, 256, 29),
+         ("C5", "rk", "depthwise_27x27_512_nhwc", 1, 14, 512, 27)]
+
+
+@pytest.mark.parametrize("name,which,fn,B,HW,C,K", TIMED, ids=[t[0] for t in TIMED])
+def test_engine_vs_reference_kernel_same_protocol(cm_ext, rk_ext, name, which, fn, B, HW, C, K):
+    """Both arms timed the same two ways on the same inputs: (a) eager, one host launch per call on
+    the current stream, as the reference's bench_custom_warm.py:17-31 does; (b) a CUDA graph of 50
+    back-to-back launches (both launch on PyTorch's current stream).  The reference's torch entry
+    points are called exactly as its ops call them (depthwise_torch_ops.py:93-124,
+    depthwise_replknet_nhwc_ops.py:71-86): the ConvMixer ones take a preallocated output, the
+    RepLKNet ones allocate it and loop over images in C++."""
+    import depthwise_conv_b200 as eng
+    gen = torch.Generator(device="cuda").manual_seed(5 + K)
+    x = torch.randn((B, HW, HW, C), generator=gen, device="cuda", dtype=torch.float16).permute(0, 3, 1, 2)
+    w = (torch.randn((K, K, C), generator=gen, device="cuda") / K).half()
+    y = torch.empty_like(x)
+    empty_bias = torch.empty(0, dtype=torch.float16, device="cuda")
+    if which == "cm":
+        ext = cm_ext
+        ref_call = lambda: getattr(ext, fn)(x, w, y, HW, HW, C, K)  # noqa: E731
+        if fn != "depthwise_forward_32_1536_9":  # one image per call: the reference op loops in Python
+            ref_call = lambda: [getattr(ext, fn)(x[b:b + 1], w, y[b:b + 1], HW, HW, C, K) for b in range(B)]  # noqa: E731
+    else:
+        ext = rk_ext
+        ref_call = lambda: getattr(ext, fn)(x, w, empty_bias)  # noqa: E731
+    ours = lambda: eng.conv2d_nhwc_fused(x, w, out=y)  # noqa: E731
+    res = {"config": name, "B": B, "HW": HW, "C": C, "K": K,
+           "ref_eager_us": _eager_us(ref_call), "ours_eager_us": _eager_us(ours)}
+    try:
+        res["ref_graph_us"] = _graph_us(ref_call)
+    except RuntimeError as e:  # a reference entry point that cannot be captured: eager numbers only
+        res["ref_graph_us"] = None
+        res["ref_graph_error"] = str(e).splitlines()[0][:120]
+    res["ours_graph_us"] = _graph_us(ours)
+    print("REFTIMING " + json.dumps(res))
+    assert res["ours_eager_us"] > 0 and res["ref_eager_us"] > 0

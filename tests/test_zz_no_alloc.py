@@ -6,7 +6,9 @@ allocation).  dwb_conv2d_nhwc_bwd_data_noalloc serves them: it takes the
 unrotated weights and keeps the rotated taps in a buffer built into the
 library.  Called here through the C ABI, twice in a row with different data,
 and compared with the allocating path (dwb_weight_rot180 into a caller buffer
-+ dwb_conv2d_nhwc_bwd_data) within the parity bar; a request larger than the
++ dwb_conv2d_nhwc_bwd_data), which runs the same kernel on the same rotated
+taps and so must agree bit for bit, and with the exact float64 adjoint of
+the oracle within the parity bar; a request larger than the
 built-in buffer is refused with a message.  This file is collected last.
 """
 from __future__ import annotations
@@ -43,9 +45,13 @@ def test_input_gradient_without_allocation_matches_allocating_path(oracle_mod):
                                                   stream)
         assert rc == _lib.OK, _lib.load().dwb_status_string(rc)
         torch.cuda.synchronize()
+        # the same kernel on the same rotated taps: bit-identical to the allocating path
+        assert torch.equal(dx, expect), f"call {call}: differs from the allocating path"
+        # and within the parity bar of the exact (float64) adjoint
+        x0 = np.zeros((B, H, W, C), np.float16)
+        exact_dx, _, _ = oracle_mod.dw_backward_numpy(x0, w, dy)
         a = dx.permute(0, 2, 3, 1).contiguous().cpu().numpy().astype(np.float64)
-        e = expect.permute(0, 2, 3, 1).contiguous().cpu().numpy().astype(np.float64)
-        max_err, rel = oracle_mod.parity(a, e)
+        max_err, rel = oracle_mod.parity(a, exact_dx)
         assert max_err <= MAX_TOL and rel <= REL_TOL, f"call {call}: max {max_err:.3e} rel {rel:.3e}"
     assert d.device_error() == 0
 
