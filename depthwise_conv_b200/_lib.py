@@ -13,6 +13,8 @@ import threading
 PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(PKG_DIR, "libdwconv_b200.so")
 
+ABI_VERSION = 5  # DWB_ABI_VERSION of include/dwconv_b200.h
+
 # dwb_status
 OK = 0
 ERR_NULL_POINTER = 1
@@ -46,7 +48,8 @@ class Plan(ctypes.Structure):
                 ("ring_rows", ctypes.c_int32), ("ring_wrows", ctypes.c_int32), ("consumer_warps", ctypes.c_int32),
                 ("threads", ctypes.c_int32), ("smem_bytes", ctypes.c_int32), ("ctas_per_sm", ctypes.c_int32),
                 ("grid", ctypes.c_int64), ("tiles", ctypes.c_int64), ("accum", ctypes.c_int32), ("regs_estimate", ctypes.c_int32),
-                ("model_cost", ctypes.c_double), ("row_splits", ctypes.c_int32), ("load_schedule", ctypes.c_int32)]
+                ("model_cost", ctypes.c_double), ("row_splits", ctypes.c_int32), ("load_schedule", ctypes.c_int32),
+                ("band_tiles", ctypes.c_int32)]
 
     def as_dict(self) -> dict:
         return {name: getattr(self, name) for name, _ in self._fields_}
@@ -123,7 +126,7 @@ def load() -> ctypes.CDLL:
                 fn = getattr(lib, name)
                 fn.argtypes = argtypes
                 fn.restype = restype
-            if lib.dwb_abi_version() != 4:
+            if lib.dwb_abi_version() != ABI_VERSION:
                 raise RuntimeError("depthwise_conv_b200: ABI version mismatch")
             _lib = lib
     return _lib

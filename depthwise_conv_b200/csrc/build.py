@@ -11,12 +11,13 @@ header is newer.  The library depends on the CUDA runtime only (no torch).
 
 Register caps.  How many warps an SM holds is set by the registers per
 thread in steps (64, 72, 80, 96, 128, 168, 255 registers = 8 ... 2 warps per
-sub-partition), and ptxas often lands a few registers above a step.
-``--regcaps`` compiles every kernel variant uncapped, reads the register
-counts ptxas reports, caps each variant that is at most 10 registers above a
-step at that step (``__maxnreg__``), recompiles, and uncaps any capped variant
-that then spills more than 32 bytes.  The result is ``dw_regcaps.inc``, committed with the
-sources; a plain build uses it.
+sub-partition), and ptxas's own choice often lands above a step it could reach
+with no or almost no spilling.  ``--regcaps`` compiles every kernel variant
+uncapped and then at each step below its natural count (``__maxnreg__``),
+reads the registers and spill bytes ptxas reports, and caps each variant at
+the lowest step where it spills at most 16 bytes of stores and 16 bytes of
+loads (a few loop-invariant words).  The result is ``dw_regcaps.inc``,
+committed with the sources; a plain build uses it.
 """
 from __future__ import annotations
 
@@ -94,33 +95,52 @@ def build(verbose: bool = False, jobs: int | None = None) -> str:
 
 
 REGCAPS = os.path.join(HERE, "dw_regcaps.inc")
-_STEPS = (64, 72, 80, 96, 128, 168, 255)
-_SPILL_OK = 32  # bytes of spill stores a cap may cost (a few loop-invariant words)
+_STEPS = (64, 72, 80, 96, 128, 168)
+_SPILL_STORES_OK = 16  # bytes of spill a cap may cost (a few loop-invariant words)
+_SPILL_LOADS_OK = 16
 _ENTRY = re.compile(r"Compiling entry function '\S*dw_stream_kernel(?:_capped)?ILi(\d+)ELi(\d+)ELi(\d+)ELi(\d+)ELi(\d+)E")
 _USED = re.compile(r"Used (\d+) registers")
-_SPILL = re.compile(r"(\d+) bytes spill stores")
+_SPILL = re.compile(r"(\d+) bytes spill stores, (\d+) bytes spill loads")
 
 
 def _ptxas_report(src: str, extra: list[str]) -> dict:
-    """{(K, R, M, acc, pre): (registers, spill bytes)} of the kernel variants in one source file."""
+    """{(K, R, M, acc, pre): (registers, spill store bytes, spill load bytes)} of one source file."""
     cmd = [_nvcc(), *ARCH, *NVCC_FLAGS, *extra, "-Xptxas", "-v", "-I", INCLUDE, "-c", src, "-o", os.devnull]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"compile failed: {' '.join(cmd)}\n{res.stdout}\n{res.stderr}")
-    out, key, spill = {}, None, 0
+    out, key, spill = {}, None, (0, 0)
     for line in res.stderr.splitlines():
         m = _ENTRY.search(line)
         if m:
-            key, spill = tuple(int(v) for v in m.groups()), 0
+            key, spill = tuple(int(v) for v in m.groups()), (0, 0)
             continue
         m = _SPILL.search(line)
         if m and key:
-            spill = int(m.group(1))
+            spill = (int(m.group(1)), int(m.group(2)))
         m = _USED.search(line)
         if m and key:
-            out[key] = (int(m.group(1)), spill)
+            out[key] = (int(m.group(1)), *spill)
             key = None
     return out
+
+
+def choose_caps(reports: dict) -> dict:
+    """reports: {cap (255 = uncapped): {variant: (regs, spill stores, spill loads)}} -> {variant: cap}.
+
+    The lowest step below the uncapped count whose spills stay within the allowance; 255 (no cap)
+    when no step qualifies."""
+    caps = {}
+    for key, (natural, _, _) in reports[255].items():
+        caps[key] = 255
+        for step in _STEPS:
+            if step >= natural or step not in reports or key not in reports[step]:
+                continue
+            regs, st, ld = reports[step][key]
+            if regs <= step and st <= _SPILL_STORES_OK and ld <= _SPILL_LOADS_OK:
+                caps[key] = step
+                break
+    return caps
 
 
 def _reports(extra: list[str]) -> dict:
@@ -132,7 +152,7 @@ def _reports(extra: list[str]) -> dict:
     return merged
 
 
-def _write_caps(caps: dict) -> None:
+def write_caps(caps: dict) -> None:
     lines = ["// dw_regcaps.inc -- per-variant register caps, generated by build.py --regcaps.",
              "// {K, R, M, ACC, PRE, max registers}"]
     lines += ["{%d, %d, %d, %d, %d, %d}," % (*k, c) for k, c in sorted(caps.items()) if c < 255]
@@ -141,23 +161,17 @@ def _write_caps(caps: dict) -> None:
 
 
 def regcaps(verbose: bool = False) -> dict:
-    """Regenerate dw_regcaps.inc from ptxas's register counts (see the module docstring)."""
-    natural = _reports(["-DDWB_NO_REGCAPS"])
-    caps = {}
-    for key, (regs, _) in natural.items():
-        step = max(b for b in _STEPS if b <= regs) if regs >= _STEPS[0] else regs
-        caps[key] = step if (regs > step and regs - step <= 10) else 255
-    _write_caps(caps)
-    capped = _reports([])
-    for key, (regs, spill) in capped.items():
-        if caps.get(key, 255) < 255 and spill > _SPILL_OK:
-            caps[key] = 255  # the cap made ptxas spill more than a few words: leave this variant alone
-    _write_caps(caps)
+    """Regenerate dw_regcaps.inc from ptxas's register and spill counts (see the module docstring)."""
+    reports = {255: _reports(["-DDWB_NO_REGCAPS"])}
+    for step in _STEPS:
+        reports[step] = _reports([f"-DDWB_FORCE_CAP={step}"])
+    caps = choose_caps(reports)
+    write_caps(caps)
     if verbose:
         for key in sorted(caps):
             if caps[key] < 255:
                 print(f"K={key[0]} R={key[1]} M={key[2]} acc={key[3]} pre={key[4]}: "
-                      f"{natural[key][0]} -> {capped[key][0]} registers")
+                      f"{reports[255][key][0]} -> {caps[key]} registers")
     return caps
 
 

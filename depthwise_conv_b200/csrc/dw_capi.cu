@@ -86,7 +86,7 @@ __global__ void bounded_wait_selftest(int* err, long long limit) {
 static __device__ int g_device_error;
 
 constexpr int kMaxDevices = 64;
-constexpr int kMaxVariants = 16 * kNumVariantR * 8;  // K values x R x M x accum x load schedule
+constexpr int kMaxVariants = 2 * 16 * kNumVariantR * 8;  // (tile, band) x K values x R x M x accum x load schedule
 
 struct VariantState {
   int regs = -1;         // -1 unknown, 0 unavailable
@@ -123,12 +123,12 @@ static int driver_fail(const char* what, int code) {
 
 static DeviceState g_devices[kMaxDevices];
 
-static int variant_slot(int K, int R, int M, int acc, int pre) {
+static int variant_slot(int K, int R, int M, int acc, int pre, bool band = false) {
   int ri = 0;
   for (; ri < kNumVariantR - 1; ++ri)
     if (kVariantR[ri] == R) break;
   const int mi = (M == 2) ? 0 : 1;
-  return ((K / 2) * kNumVariantR + ri) * 8 + mi * 4 + acc * 2 + (pre ? 1 : 0);
+  return (((band ? 16 : 0) + K / 2) * kNumVariantR + ri) * 8 + mi * 4 + acc * 2 + (pre ? 1 : 0);
 }
 
 static void init_device(int dev, DeviceState* st) {
@@ -188,11 +188,12 @@ static int regs_of_variant(int K, int R, int M, int acc, int pre, void* ctx) {
   return vs.regs;
 }
 
-static int ensure_smem_attr(DeviceState* st, const KernelEntry* e, int smem) {
-  VariantState& vs = st->variants[variant_slot(e->k, e->r, e->m, e->acc, e->pre)];
+static int ensure_smem_attr(DeviceState* st, const KernelEntry* e, bool band, int smem) {
+  VariantState& vs = st->variants[variant_slot(e->k, e->r, e->m, e->acc, e->pre, band)];
   std::lock_guard<std::mutex> lk(st->mu);
   if (vs.smem_max >= smem) return DWB_OK;
-  const cudaError_t ce = cudaFuncSetAttribute(e->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  const cudaError_t ce =
+      cudaFuncSetAttribute(band ? e->band : e->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (ce != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(MaxDynamicSharedMemorySize)", ce);
   vs.smem_max = smem;
   return DWB_OK;
@@ -230,13 +231,14 @@ static int encode_x_map(CUtensorMap* m, const void* x, long long B, long long H,
   return r == CUDA_SUCCESS ? DWB_OK : driver_fail("cuTensorMapEncodeTiled(x)", static_cast<int>(r));
 }
 
-// w: [K][K][C] fp16 viewed as (C, K, K); box = 64 channels x K taps x 1 row.
-static int encode_w_map(CUtensorMap* m, const void* w, long long C, int K) {
+// w: [K][K][C] fp16 viewed as (C, K, K); box = 64 channels x K taps x `rows` kernel rows
+// (1: one weight row per stage; K: all of a channel block's taps at once, band mode).
+static int encode_w_map(CUtensorMap* m, const void* w, long long C, int K, int rows = 1) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return driver_fail("cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)", -1);
   const cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)K, (cuuint64_t)K};
   const cuuint64_t strides[2] = {(cuuint64_t)(C * 2), (cuuint64_t)(K * C * 2)};
-  const cuuint32_t box[3] = {(cuuint32_t)kChannelsPerCta, (cuuint32_t)K, 1};
+  const cuuint32_t box[3] = {(cuuint32_t)kChannelsPerCta, (cuuint32_t)K, (cuuint32_t)rows};
   const cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(w), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -281,13 +283,16 @@ static int launch_plan(DeviceState* st, const dwb_plan& plan, const void* x, con
                        long long W, long long C, int K, int act, void* stream) {
   const KernelEntry* e = find_variant(K, plan.cols_per_thread, plan.rows_per_thread, plan.accum, plan.load_schedule);
   if (!e) return DWB_ERR_UNSUPPORTED;
-  int rc = ensure_smem_attr(st, e, plan.smem_bytes);
+  const bool band = plan.band_tiles > 0;
+  if (band && !e->band) return DWB_ERR_UNSUPPORTED;
+  const void* fn = band ? e->band : e->fn;
+  int rc = ensure_smem_attr(st, e, band, plan.smem_bytes);
   if (rc != DWB_OK) return rc;
 
   CUtensorMap tmx, tmw;
   rc = encode_x_map(&tmx, x, B, H, W, C, plan.tile_w_in);
   if (rc != DWB_OK) return rc;
-  rc = encode_w_map(&tmw, w, C, K);
+  rc = encode_w_map(&tmw, w, C, K, band ? K : 1);
   if (rc != DWB_OK) return rc;
 
   DwParams p;
@@ -316,25 +321,34 @@ static int launch_plan(DeviceState* st, const dwb_plan& plan, const void* x, con
   p.stages = plan.ring_rows;
   p.act = act;
   p.ring_off = kBarrierBytes;
-  p.stage_bytes = static_cast<uint32_t>(plan.tile_w_in + K) * kPixelBytes;
-  long long red_off = 0;
-  const long long smem_need = plan_smem_bytes(K, plan.tile_w_in, plan.ring_rows, p.nsplit, p.slots,
-                                              plan.rows_per_thread, plan.cols_per_thread, &red_off);
+  // a stage holds one staged input row (band mode) or an input row and a weight row
+  p.stage_bytes = static_cast<uint32_t>(plan.tile_w_in + (band ? 0 : K)) * kPixelBytes;
+  long long red_off = 0, wbuf_off = 0;
+  const long long smem_need =
+      band ? band_smem_bytes(K, plan.tile_w_in, plan.ring_rows, p.nsplit, p.slots, plan.rows_per_thread,
+                             plan.cols_per_thread, &red_off, &wbuf_off)
+           : plan_smem_bytes(K, plan.tile_w_in, plan.ring_rows, p.nsplit, p.slots, plan.rows_per_thread,
+                             plan.cols_per_thread, &red_off);
   if (smem_need > plan.smem_bytes) return DWB_ERR_BAD_ARG;
   p.red_off = static_cast<uint32_t>(red_off);
+  p.wbuf_off = static_cast<uint32_t>(wbuf_off);
+  p.band_tiles = band ? plan.band_tiles : 0;
+  p.bands_h = band ? static_cast<int>((p.tiles_h + plan.band_tiles - 1) / plan.band_tiles) : 0;
+  p.num_bands = band ? static_cast<uint32_t>(plan.tiles) : 0u;
   p.err = st->err_word;
+  p.res_in_ring = 0;  // set below, once the grid is known
 
   // grid < 0: persistent, as many CTAs as fit on the device at once (measured
   // by the occupancy calculator for this variant); otherwise the plan's CTA
   // count (one tile per CTA when it equals the tile count).
   long long grid = plan.grid;
   {
-    VariantState& vs = st->variants[variant_slot(e->k, e->r, e->m, e->acc, e->pre)];
+    VariantState& vs = st->variants[variant_slot(e->k, e->r, e->m, e->acc, e->pre, band)];
     std::lock_guard<std::mutex> lk(st->mu);
     if (vs.occ_threads != plan.threads || vs.occ_smem != plan.smem_bytes) {
       int occ = 0;
       const cudaError_t oe =
-          cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, e->fn, plan.threads, static_cast<size_t>(plan.smem_bytes));
+          cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, plan.threads, static_cast<size_t>(plan.smem_bytes));
       if (oe != cudaSuccess) return cuda_fail("cudaOccupancyMaxActiveBlocksPerMultiprocessor", oe);
       vs.occ_threads = plan.threads;
       vs.occ_smem = plan.smem_bytes;
@@ -346,12 +360,17 @@ static int launch_plan(DeviceState* st, const dwb_plan& plan, const void* x, con
     if (grid <= 0 || grid > plan.tiles) grid = plan.tiles;
   }
 
+  // A ConvMixer block's residual is the convolution's own input: when every CTA runs exactly one
+  // tile and the ring holds all of that tile's input rows (nothing is ever refilled), the epilogue
+  // reads it from shared memory.
+  p.res_in_ring = (!band && residual != nullptr && residual == x && grid == plan.tiles &&
+                   plan.ring_rows >= plan.tile_h + K - 1) ? 1 : 0;
   void* args[3] = {&tmx, &tmw, &p};
-  const cudaError_t ce = launch_kernel(e->fn, dim3(static_cast<unsigned>(grid)), dim3(plan.threads), args,
+  const cudaError_t ce = launch_kernel(fn, dim3(static_cast<unsigned>(grid)), dim3(plan.threads), args,
                                        static_cast<size_t>(plan.smem_bytes), static_cast<cudaStream_t>(stream));
   if (ce != cudaSuccess) {
     (void)cudaGetLastError();
-    return cuda_fail("cudaLaunchKernelExC(dw_stream_kernel)", ce);
+    return cuda_fail(band ? "cudaLaunchKernelExC(dw_band_kernel)" : "cudaLaunchKernelExC(dw_stream_kernel)", ce);
   }
   return DWB_OK;
 }
@@ -365,6 +384,7 @@ struct TunedPlan {
   int K, accum, R, M, tile_h, tile_w, ring_rows, ring_wrows, grid;
   int splits;  // row split (0 or 1 = none)
   int pre;     // load schedule
+  int band;    // band mode: row tiles per band (0 = tile mode)
 };
 static const TunedPlan kTunedPlans[] = {
 #include "dw_tuned_plans.inc"
@@ -396,6 +416,7 @@ static bool tuned_plan(DeviceState* st, const dwb_problem& pr, dwb_plan* out) {
   p.grid = best->grid;
   p.row_splits = best->splits;
   p.load_schedule = best->pre;
+  p.band_tiles = best->band;
   const int regs = regs_of_variant(p.kernel_size, p.cols_per_thread, p.rows_per_thread, p.accum, p.load_schedule, st);
   if (regs <= 0 || check_plan(pr, st->hw, regs, &p) != DWB_OK) return false;
   p.ctas_per_sm = 0;  // not modelled for tuned plans

@@ -35,6 +35,8 @@ bool variant_compiled(int K, int R, int M, int acc, int pre) {
 }
 const int kVariantM[2] = {2, 1};
 
+bool band_compiled(int K, int acc) { return acc == DWB_ACCUM_MIXED && K <= kBandMaxK; }
+
 int default_load_schedule(int K, int R, int M, int acc) {
   (void)R;
   (void)M;
@@ -48,9 +50,13 @@ namespace {
 constexpr int kChannelsPerCta = 64;
 constexpr int kPixelBytes = 128;
 constexpr int kBarrierBytes = 1024;
-constexpr int kMaxConsumerWarps = 16;
+constexpr int kMaxConsumerWarps = 31;  // a CTA of at most 32 warps (1024 threads) with its producer
 constexpr int kMaxBoxDim = 256;  // TMA box limit per dimension
 constexpr double kLoadLatency = 2000.0;  // clocks from TMA issue to data (L2/HBM), modelled
+// TMA tile loads of 64-channel NHWC pixels: one 128-byte request per staged
+// pixel, about 8 clocks each per SM (measured on B200 from the issue times of
+// back-to-back row loads), i.e. ~16 bytes per clock per SM
+constexpr double kTmaBytesPerClk = 16.0;
 constexpr int kNumSplits = 5;
 constexpr int kSplits[kNumSplits] = {1, 2, 3, 4, 8};  // row splits the planner considers
 
@@ -89,7 +95,17 @@ long long plan_smem_bytes(int K, int tile_w_in, int stages, int nsplit, int slot
   return off;
 }
 
-bool barriers_fit(int stages) { return (2 * stages + 2) * 8 <= kBarrierBytes; }
+long long band_smem_bytes(int K, int tile_w_in, int stages, int nsplit, int slots, int M, int R, long long* red_off,
+                          long long* wbuf_off) {
+  long long off = kBarrierBytes + static_cast<long long>(stages) * tile_w_in * kPixelBytes;
+  if (red_off) *red_off = off;
+  if (nsplit > 1) off += static_cast<long long>(nsplit - 1) * slots * M * R * 32 * 8;
+  off = (off + 127) / 128 * 128;
+  if (wbuf_off) *wbuf_off = off;
+  return off + 2LL * K * K * kPixelBytes;
+}
+
+bool barriers_fit(int stages, bool band) { return (2 * stages + 2 + (band ? 4 : 0)) * 8 <= kBarrierBytes; }
 
 int validate_problem(const dwb_problem& pr) {
   const long long B = pr.batch, H = pr.height, W = pr.width, C = pr.channels;
@@ -195,7 +211,7 @@ int enumerate_plans(const dwb_problem& pr, const HwInfo& hw, RegsFn regs, void* 
                                 : warps_per_smsp >= 1.0 ? 0.65
                                                         : 0.65 * warps_per_smsp;
             const double t_tp = std::max(static_cast<double>(tiles_busiest) * work_cta / (4.0 * util),
-                                         static_cast<double>(tiles_busiest) * bytes_cta / 64.0);
+                                         static_cast<double>(tiles_busiest) * bytes_cta / kTmaBytesPerClk);
             // a persistent CTA pays the load latency once, then once per step it
             // cannot prefetch far enough ahead
             const double tiles_per_cta = std::ceil(static_cast<double>(tiles) / static_cast<double>(grid));
@@ -226,8 +242,77 @@ int enumerate_plans(const dwb_problem& pr, const HwInfo& hw, RegsFn regs, void* 
           pl.model_cost = cost;
           pl.row_splits = nsplit;
           pl.load_schedule = pre;
+          pl.band_tiles = 0;
           ++count;
           if (sink) sink(pl, sink_ctx);
+          }
+
+          // Band mode: a CTA streams bands of bt row tiles, every input row once
+          // per band and the K x K weights once (mixed accumulation, small K).
+          if (band_compiled(K, pr.accum)) {
+            const long long bts[4] = {2, 4, 8, tiles_h};
+            long long last_bt = -1;
+            for (int bi = 0; bi < 4; ++bi) {
+              const long long bt = std::min<long long>(bts[bi], tiles_h);
+              if (bt == last_bt) continue;
+              last_bt = bt;
+              const long long bands_h = ceil_div(tiles_h, bt);
+              const long long bands = B * cblocks * tiles_w * bands_h;
+              if (bands > 0x7fffffffLL || bands < 1) continue;
+              const double band_rows = std::min<double>(static_cast<double>(bt * tile_h), static_cast<double>(H));
+              const double bytes_band = ((band_rows + K - 1) * tile_w_in + static_cast<double>(K) * K) * kPixelBytes;
+              const double work_band = work_cta * static_cast<double>(bt);
+              const long long bands_busiest = ceil_div(bands, hw.sm_count);
+              for (int extra = 0; extra <= 8; extra += 4) {
+                const int ring_rows = tile_h + K - 1 + extra;
+                long long red_off = 0, wbuf_off = 0;
+                const long long smem = band_smem_bytes(K, tile_w_in, ring_rows, nsplit, slots, M, R, &red_off, &wbuf_off);
+                if (smem > hw.smem_optin || !barriers_fit(ring_rows, true)) break;
+                const int cps = static_cast<int>(std::min<long long>(
+                    {hw.smem_per_sm / (smem + hw.smem_reserved), static_cast<long long>(cps_regs),
+                     hw.max_threads_sm / threads, hw.max_ctas_sm}));
+                if (cps < 1) continue;
+                const long long grid = std::min<long long>(bands, static_cast<long long>(cps) * hw.sm_count);
+                const long long resident = std::min<long long>(cps, bands_busiest);
+                const double warps_per_smsp = static_cast<double>(resident * consumer_warps) / 4.0;
+                const double util = warps_per_smsp >= 3.0   ? 1.0
+                                    : warps_per_smsp >= 2.0 ? 0.9
+                                    : warps_per_smsp >= 1.0 ? 0.65
+                                                            : 0.65 * warps_per_smsp;
+                const double t_tp = std::max(static_cast<double>(bands_busiest) * work_band / (4.0 * util),
+                                             static_cast<double>(bands_busiest) * bytes_band / kTmaBytesPerClk);
+                const double bands_per_cta = std::ceil(static_cast<double>(bands) / static_cast<double>(grid));
+                const double ahead = static_cast<double>(extra + 1);  // rows the producer runs ahead of a window
+                const double t_lat = kLoadLatency + bands_per_cta * static_cast<double>(bt) *
+                                                        (static_cast<double>(K) * kLoadLatency / (ahead * K) + 300.0);
+                const double t_warp = bands_per_cta * work_band / consumer_warps;
+                const double cost = std::max({t_tp, t_lat, t_warp}) + bands_per_cta * static_cast<double>(bt) * 300.0;
+                dwb_plan pl;
+                std::memset(&pl, 0, sizeof(pl));
+                pl.kernel_size = K;
+                pl.cols_per_thread = R;
+                pl.rows_per_thread = M;
+                pl.channel_block = kChannelsPerCta;
+                pl.tile_h = tile_h;
+                pl.tile_w = tile_w;
+                pl.tile_w_in = tile_w_in;
+                pl.ring_rows = ring_rows;
+                pl.consumer_warps = consumer_warps;
+                pl.threads = threads;
+                pl.smem_bytes = static_cast<int32_t>(smem);
+                pl.ctas_per_sm = cps;
+                pl.grid = grid;
+                pl.tiles = bands;
+                pl.accum = pr.accum;
+                pl.regs_estimate = rg;
+                pl.model_cost = cost;
+                pl.row_splits = nsplit;
+                pl.load_schedule = pre;
+                pl.band_tiles = static_cast<int32_t>(bt);
+                ++count;
+                if (sink) sink(pl, sink_ctx);
+              }
+            }
           }
          }
         }
@@ -279,20 +364,25 @@ int check_plan(const dwb_problem& pr, const HwInfo& hw, int regs, dwb_plan* p) {
   const int slots = (p->tile_w / R) * (p->tile_h / M);
   const int cw = S * slots;
   if (slots < 1 || cw > 31) return DWB_ERR_BAD_ARG;
-  if (p->ring_rows < p->tile_h) return DWB_ERR_BAD_ARG;
-  if (!barriers_fit(p->ring_rows)) return DWB_ERR_BAD_ARG;
-  p->ring_wrows = 0;  // weight rows travel in the input-row stages
+  const bool band = p->band_tiles > 0;
+  if (p->band_tiles < 0 || (band && !band_compiled(K, p->accum))) return DWB_ERR_BAD_ARG;
+  if (p->ring_rows < (band ? p->tile_h + K - 1 : p->tile_h)) return DWB_ERR_BAD_ARG;
+  if (!barriers_fit(p->ring_rows, band)) return DWB_ERR_BAD_ARG;
+  p->ring_wrows = 0;  // weight rows travel in the input-row stages (or stay resident: band mode)
   p->channel_block = kChannelsPerCta;
   p->tile_w_in = p->tile_w + K - 1;
   p->consumer_warps = cw;
   p->threads = 32 * (cw + 1);
-  const long long smem = plan_smem_bytes(K, p->tile_w_in, p->ring_rows, S, slots, M, R, nullptr);
+  const long long smem = band ? band_smem_bytes(K, p->tile_w_in, p->ring_rows, S, slots, M, R, nullptr, nullptr)
+                              : plan_smem_bytes(K, p->tile_w_in, p->ring_rows, S, slots, M, R, nullptr);
   if (smem > hw.smem_optin) return DWB_ERR_BAD_ARG;
   if (regs > 0 && ctas_by_registers(regs, cw + 1, hw.regs_per_sm) < 1) return DWB_ERR_BAD_ARG;
   p->smem_bytes = static_cast<int32_t>(smem);
-  p->tiles = pr.batch * ceil_div(pr.height, p->tile_h) * ceil_div(pr.width, p->tile_w) *
-             ceil_div(pr.channels, kChannelsPerCta);
-  if (p->tiles > (1LL << 40)) return DWB_ERR_BAD_SHAPE;
+  const long long tiles_h = ceil_div(pr.height, p->tile_h);
+  const long long strips = pr.batch * ceil_div(pr.width, p->tile_w) * ceil_div(pr.channels, kChannelsPerCta);
+  // work units the CTAs walk: tiles, or bands of band_tiles row tiles
+  p->tiles = strips * (band ? ceil_div(tiles_h, p->band_tiles) : tiles_h);
+  if (p->tiles > (1LL << 40) || (band && p->tiles > 0x7fffffffLL)) return DWB_ERR_BAD_SHAPE;
   // grid: < 0 = persistent (sized by the launcher from the occupancy), else
   // the caller's CTA count, at most one per tile (0 = one CTA per tile)
   if (p->grid == 0 || p->grid > p->tiles) p->grid = p->tiles;

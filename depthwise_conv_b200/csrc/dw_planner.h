@@ -11,6 +11,9 @@
 
 namespace dwb {
 
+// Band-mode kernels (mixed accumulation) are built for K <= kBandMaxK.
+constexpr int kBandMaxK = 17;
+
 struct HwInfo {
   int sm_count = 148;          // B200
   int smem_optin = 232448;     // max dynamic smem per CTA (227 KB)
@@ -33,6 +36,8 @@ constexpr int kNumVariantR = 6;
 extern const int kVariantR[kNumVariantR];
 extern const int kVariantM[2];
 bool variant_compiled(int K, int R, int M, int acc, int pre);
+// Whether the variant also has a band-mode kernel (dw_variants.cuh).
+bool band_compiled(int K, int acc);
 
 // Load schedule the cost model assumes for a variant (the tuner measures both).
 int default_load_schedule(int K, int R, int M, int acc);
@@ -43,8 +48,15 @@ int default_load_schedule(int K, int R, int M, int acc);
 // *red_off receives the exchange area's byte offset.
 long long plan_smem_bytes(int K, int tile_w_in, int stages, int nsplit, int slots, int M, int R, long long* red_off);
 
-// Whether the 1 KB mbarrier area holds the ring's 2 * stages + 2 barriers.
-bool barriers_fit(int stages);
+// Dynamic shared memory of a band-mode plan: mbarriers, the stage ring (one
+// staged input row per stage), the partial-sum exchange area (S > 1), then the
+// two resident K x K weight buffers, whose byte offset goes to *wbuf_off.
+long long band_smem_bytes(int K, int tile_w_in, int stages, int nsplit, int slots, int M, int R, long long* red_off,
+                          long long* wbuf_off);
+
+// Whether the 1 KB mbarrier area holds the ring's 2 * stages + 2 barriers
+// (+ 4 for the band mode's weight buffers).
+bool barriers_fit(int stages, bool band = false);
 
 // Range checks shared by every entry point.  Returns a dwb_status.
 int validate_problem(const dwb_problem& pr);

@@ -3,12 +3,28 @@
 //   32 and 56 without overhang, plus R in {28, 32} for K <= 13, where a wider
 //   register block amortises the per-kernel-row overhead over more FMAs;
 //   M (rows per thread) in {1, 2}; ACC 0 = fp32 FFMA2, 1 = fp16x2 chains with
-//   fp32 accumulation; PRE (load schedule, mixed mode only) 0 or 1.
-//   dw_planner.cpp (variant_compiled) mirrors this list.
+//   fp32 accumulation; PRE (load schedule, mixed mode only) 0 or 1.  Each
+//   mixed-mode variant with K <= kBandMaxK also has a band-mode kernel.
+//   dw_planner.cpp (variant_compiled, band_compiled) mirrors this list.
 #pragma once
 #include "dw_kernel.cuh"
 
-#define DWB_ENTRY(K, R, M, A, P) {K, R, M, A, P, ::dwb::kernel_fn<K, R, M, A, P>()}
+namespace dwb {
+// Band-mode kernels (dw_band_body) are built for the mixed accumulation and
+// K <= kBandMaxK, where the two resident K x K weight buffers stay small and
+// TMA requests, not FMAs, bound the tile kernel.  dw_planner.cpp mirrors this.
+template <int K, int R, int M, int ACC, int PRE>
+inline const void* band_entry() {
+  if constexpr (ACC == 1 && K <= kBandMaxK) {
+    return band_kernel_fn<K, R, M, ACC, PRE>();
+  } else {
+    return nullptr;
+  }
+}
+}  // namespace dwb
+
+#define DWB_ENTRY(K, R, M, A, P) \
+  {K, R, M, A, P, ::dwb::kernel_fn<K, R, M, A, P>(), ::dwb::band_entry<K, R, M, A, P>()}
 #define DWB_VARIANTS_AP(K, A, P)                                                                            \
   DWB_ENTRY(K, 7, 1, A, P), DWB_ENTRY(K, 7, 2, A, P), DWB_ENTRY(K, 8, 1, A, P), DWB_ENTRY(K, 8, 2, A, P),   \
       DWB_ENTRY(K, 14, 1, A, P), DWB_ENTRY(K, 14, 2, A, P), DWB_ENTRY(K, 16, 1, A, P), DWB_ENTRY(K, 16, 2, A, P)

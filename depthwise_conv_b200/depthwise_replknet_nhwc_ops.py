@@ -44,14 +44,13 @@ def _replknet_op(fn: str, input, weight, bias, C: int, HW: int, K: int):
     bp = dw_ops.check_vec(bias, C, "bias", input.device)  # empty tensor = no bias (reference :73)
     output = torch.empty_like(input)
     with dw_ops._DeviceGuard(input.device):
+        stream = dw_ops._stream_of(input)
         if fn:
-            _lib.call(fn, input.data_ptr(), weight.data_ptr(), bp or None, output.data_ptr(), B, Ci, Hi, Wi,
-                      torch.cuda.current_stream(input.device).cuda_stream)
+            _lib.call(fn, input.data_ptr(), weight.data_ptr(), bp or None, output.data_ptr(), B, Ci, Hi, Wi, stream)
         else:
             _lib.call("dwb_conv2d_nhwc_fused_fwd", input.data_ptr(), weight.data_ptr(), bp or None, None, None,
-                      None, output.data_ptr(), B, Hi, Wi, Ci, K, _lib.ACT_NONE, _lib.ACCUM_DEFAULT,
-                      torch.cuda.current_stream(input.device).cuda_stream)
-        _lib.after_launch(torch.cuda.current_stream(input.device).cuda_stream, fn or "dwb_conv2d_nhwc_fused_fwd")
+                      None, output.data_ptr(), B, Hi, Wi, Ci, K, _lib.ACT_NONE, _lib.ACCUM_DEFAULT, stream)
+        _lib.after_launch(stream, fn or "dwb_conv2d_nhwc_fused_fwd")
     return output
 
 
@@ -116,6 +115,8 @@ class NHWCDepthwise31x31_128(nn.Module):
         _load_kernels()
 
     def forward(self, x):
+        if dw_ops.direct_call_ok(x, self.weight, self.bias):  # eager inference: no dispatcher round trip
+            return _replknet_op('dwb_depthwise_31x31_128_nhwc', x, self.weight, self.bias, 128, 56, 31)
         return torch.ops.replknet_dw.conv_56_128_31(x, self.weight, self.bias)
 
 
@@ -129,6 +130,8 @@ class NHWCDepthwise29x29_256(nn.Module):
         _load_kernels()
 
     def forward(self, x):
+        if dw_ops.direct_call_ok(x, self.weight, self.bias):  # eager inference: no dispatcher round trip
+            return _replknet_op('dwb_depthwise_29x29_256_nhwc', x, self.weight, self.bias, 256, 28, 29)
         return torch.ops.replknet_dw.conv_28_256_29(x, self.weight, self.bias)
 
 
@@ -142,6 +145,8 @@ class NHWCDepthwise27x27_512(nn.Module):
         _load_kernels()
 
     def forward(self, x):
+        if dw_ops.direct_call_ok(x, self.weight, self.bias):  # eager inference: no dispatcher round trip
+            return _replknet_op('dwb_depthwise_27x27_512_nhwc', x, self.weight, self.bias, 512, 14, 27)
         return torch.ops.replknet_dw.conv_14_512_27(x, self.weight, self.bias)
 
 
@@ -155,6 +160,8 @@ class NHWCDepthwise13x13_1024(nn.Module):
         _load_kernels()
 
     def forward(self, x):
+        if dw_ops.direct_call_ok(x, self.weight, self.bias):  # eager inference: no dispatcher round trip
+            return _replknet_op(None, x, self.weight, self.bias, 1024, 7, 13)
         return torch.ops.replknet_dw.conv_7_1024_13(x, self.weight, self.bias)
 
 

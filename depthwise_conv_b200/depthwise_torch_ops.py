@@ -40,7 +40,7 @@ def _load_kernels():
 
 
 def _stream(t: torch.Tensor) -> int:
-    return torch.cuda.current_stream(t.device).cuda_stream
+    return torch._C._cuda_getCurrentRawStream(t.device.index)
 
 
 def _fixed_op(fn: str, input: torch.Tensor, weight: torch.Tensor, H: int, W: int, C: int, K: int,
@@ -55,10 +55,11 @@ def _fixed_op(fn: str, input: torch.Tensor, weight: torch.Tensor, H: int, W: int
     args = [input.data_ptr(), weight.data_ptr(), output.data_ptr(), Hi, Wi, Ci, K, B]
     if with_stride:
         args.append(Hi * Wi * Ci)
-    args.append(_stream(input))
     with dw_ops._DeviceGuard(input.device):
+        stream = _stream(input)
+        args.append(stream)
         _lib.call(fn, *args)
-        _lib.after_launch(_stream(input), fn)
+        _lib.after_launch(stream, fn)
     return output
 
 
@@ -120,6 +121,15 @@ def _depthwise_conv2d_32_1536_13_fake(input, weight):
     return torch.empty_like(input)
 
 
+_FIXED_IMPL = {
+    'depthwise::conv2d_32_1536_9': _depthwise_conv2d_32_1536_9_impl,
+    'depthwise::conv2d_32_1536_9_v2': _depthwise_conv2d_32_1536_9_v2_impl,
+    'depthwise::conv2d_32_768_7': _depthwise_conv2d_32_768_7_impl,
+    'depthwise::conv2d_16_1536_9': _depthwise_conv2d_16_1536_9_impl,
+    'depthwise::conv2d_32_1536_13': _depthwise_conv2d_32_1536_13_impl,
+}
+
+
 class CustomDepthwiseConv2d(nn.Module):
     """Depthwise conv on the B200 engine; drop-in for the reference module (:162-265).
 
@@ -170,6 +180,12 @@ class CustomDepthwiseConv2d(nn.Module):
         if self.spatial_size is None:
             self.spatial_size = H
             self.op_name = self._get_op_name(H)
+        if dw_ops.direct_call_ok(x, self.weight, self.bias):
+            # eager inference: the op's own implementation, without the dispatcher round trip
+            # (the same kernel launch; torch.compile and autograd keep going through the ops)
+            if self.bias is not None or self.op_name == 'depthwise::conv2d_nhwc':
+                return dw_ops.conv2d_nhwc_fused(x, self.weight, bias=self.bias)
+            return _FIXED_IMPL[self.op_name](x, self.weight)
         if self.bias is not None or self.op_name == 'depthwise::conv2d_nhwc':
             # bias fused into the kernel epilogue (one launch instead of conv + add)
             return torch.ops.depthwise.conv2d_nhwc(x, self.weight, self.bias)

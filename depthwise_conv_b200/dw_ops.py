@@ -35,7 +35,8 @@ ACT_CODES = _lib.ACT_CODES
 
 
 def _stream_of(t: torch.Tensor) -> int:
-    return torch.cuda.current_stream(t.device).cuda_stream
+    """Raw handle of PyTorch's current stream on the tensor's device (no Stream object is built)."""
+    return torch._C._cuda_getCurrentRawStream(t.device.index)
 
 
 def check_input(x: torch.Tensor, name: str = "input") -> None:
@@ -70,12 +71,14 @@ def check_vec(v, C: int, name: str, device) -> int:
 class _DeviceGuard:
     """Make the tensor's device current for the C ABI (cheap when it already is)."""
 
+    __slots__ = ("idx", "prev")
+
     def __init__(self, device: torch.device):
         self.idx = device.index
         self.prev = None
 
     def __enter__(self):
-        cur = torch.cuda.current_device()
+        cur = torch._C._cuda_getDevice()
         if cur != self.idx:
             self.prev = cur
             torch.cuda.set_device(self.idx)
@@ -83,6 +86,18 @@ class _DeviceGuard:
     def __exit__(self, *exc):
         if self.prev is not None:
             torch.cuda.set_device(self.prev)
+
+
+def direct_call_ok(*tensors) -> bool:
+    """Whether a module may call the op's implementation directly instead of through torch.ops:
+    eager mode (not tracing for torch.compile) and no gradient needed for any of ``tensors``."""
+    if torch.compiler.is_compiling():
+        return False
+    if torch.is_grad_enabled():
+        for t in tensors:
+            if t is not None and t.requires_grad:
+                return False
+    return True
 
 
 def conv2d_nhwc_fused(x: torch.Tensor, w: torch.Tensor, bias=None, scale=None, shift=None, residual=None,
@@ -117,15 +132,15 @@ def conv2d_nhwc_fused(x: torch.Tensor, w: torch.Tensor, bias=None, scale=None, s
         if out.shape != x.shape:
             raise RuntimeError("out must match input in shape")
     with _DeviceGuard(x.device):
+        stream = _stream_of(x)
         if plan is None:
             _lib.call("dwb_conv2d_nhwc_fused_fwd", x.data_ptr(), w.data_ptr(), bp or None, sp or None, hp or None,
-                      rp or None, y.data_ptr(), B, H, W, C, K, act_code, int(accum), _stream_of(x))
+                      rp or None, y.data_ptr(), B, H, W, C, K, act_code, int(accum), stream)
         else:
             pl = _lib.Plan.from_dict(plan)
             _lib.call("dwb_conv2d_nhwc_fwd_planned", x.data_ptr(), w.data_ptr(), bp or None, sp or None,
-                      hp or None, rp or None, y.data_ptr(), B, H, W, C, K, act_code, ctypes.byref(pl),
-                      _stream_of(x))
-        _lib.after_launch(_stream_of(x), "depthwise conv2d_nhwc_fused")
+                      hp or None, rp or None, y.data_ptr(), B, H, W, C, K, act_code, ctypes.byref(pl), stream)
+        _lib.after_launch(stream, "depthwise conv2d_nhwc_fused")
     return y
 
 

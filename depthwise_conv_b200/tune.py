@@ -16,6 +16,7 @@ are also printed as JSON lines.
 from __future__ import annotations
 
 import argparse
+import itertools
 import json
 import os
 import time
@@ -31,7 +32,7 @@ DEFAULT_PROBLEMS = [
 ] + [(64, 56, 56, 1024, k) for k in (7, 9, 13, 17, 21, 27, 29, 31)]
 
 FIELDS = ("cols_per_thread", "rows_per_thread", "tile_h", "tile_w", "ring_rows", "ring_wrows", "grid", "row_splits",
-          "load_schedule")
+          "load_schedule", "band_tiles")
 
 
 EPILOGUE = {}  # keyword arguments of the fused op while timing (set by --epilogue)
@@ -91,7 +92,12 @@ def tune_problem(B, H, W, C, K, accum, budget, proxy_batch=8, finalists=8):
     import depthwise_conv_b200 as d
     from depthwise_conv_b200 import _lib
 
-    cands = sorted(_lib.plan_candidates(B, H, W, C, K, accum), key=lambda c: c["model_cost"])
+    # the cost model ranks within a mode far better than across the tile and band modes, so the two
+    # modes' candidates are interleaved, each in model order
+    allc = _lib.plan_candidates(B, H, W, C, K, accum)
+    by_mode = [sorted((c for c in allc if (c["band_tiles"] > 0) == band), key=lambda c: c["model_cost"])
+               for band in (False, True)]
+    cands = [c for pair in itertools.zip_longest(*by_mode) for c in pair if c is not None]
     Bp = min(B, proxy_batch)
     xp, wp, yp = _inputs(Bp, H, W, C, K)
     ranked = []
@@ -134,7 +140,7 @@ def tune_problem(B, H, W, C, K, accum, budget, proxy_batch=8, finalists=8):
 def write_table(rows, path):
     lines = ["// dw_tuned_plans.inc -- plans measured fastest on B200 by depthwise_conv_b200/tune.py.",
              "// {B, H, W, C, K, accum, R, M, tile_h, tile_w, ring_rows, ring_wrows, grid(-1 persistent, 0 one tile/CTA),",
-             "//  row_splits, load_schedule}"]
+             "//  row_splits, load_schedule, band_tiles (0 = tile mode)}"]
     old = []
     if os.path.exists(TABLE):  # start from the committed table
         for ln in open(TABLE):

@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define DWB_ABI_VERSION 4
+#define DWB_ABI_VERSION 5
 
 #if defined(__GNUC__)
 #define DWB_API __attribute__((visibility("default")))
@@ -90,7 +90,8 @@ typedef struct dwb_plan {
     int32_t smem_bytes;
     int32_t ctas_per_sm;
     int64_t grid;               /* CTAs launched (persistent: <= tiles)         */
-    int64_t tiles;              /* output tiles, walked by the CTAs in strides  */
+    int64_t tiles;              /* work units the CTAs walk in strides: output
+                                   tiles, or (band mode) bands                  */
     int32_t accum;              /* dwb_accum actually used                      */
     int32_t regs_estimate;      /* registers/thread assumed by the planner      */
     double model_cost;          /* planner's modelled time (arbitrary units)     */
@@ -100,6 +101,13 @@ typedef struct dwb_plan {
     int32_t load_schedule;      /* 0: input columns read next to their FMAs;
                                    1: the row segment read into registers first
                                    (mixed accumulation only)                     */
+    int32_t band_tiles;         /* 0: every tile stages its own tile_h + K - 1
+                                   input rows and K weight rows.  n > 0 (band
+                                   mode, mixed accumulation, K <= 17): a CTA
+                                   walks bands of n row tiles of one column
+                                   strip, staging each input row once per band
+                                   and the K x K weights once; ring_rows must be
+                                   at least tile_h + K - 1                      */
 } dwb_plan;
 
 /* ---- library information ------------------------------------------------ */

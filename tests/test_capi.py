@@ -39,7 +39,7 @@ def test_every_declared_symbol_is_exported_and_bound(lib):
 
 def test_abi_version_and_status_strings(lib):
     from depthwise_conv_b200 import _lib
-    assert lib.dwb_abi_version() == 4
+    assert lib.dwb_abi_version() == 5
     for code in range(9):
         assert lib.dwb_status_string(code) and b"unknown" not in lib.dwb_status_string(code)
     assert lib.dwb_status_string(99) == b"unknown status"
@@ -124,13 +124,24 @@ def test_plans_respect_hardware_limits(B, H, W, C, K, accum):
     per_warp = -(-p["regs_estimate"] * 32 // 256) * 256
     assert -(-(p["consumer_warps"] + 1) // 4) * per_warp <= 16384
     assert p["smem_bytes"] <= 232448 and p["ctas_per_sm"] >= 1
-    assert p["ring_rows"] >= p["tile_h"] and p["ring_wrows"] == 0
-    assert (2 * p["ring_rows"] + 2) * 8 <= 1024  # mbarrier area
-    ring = 1024 + p["ring_rows"] * (p["tile_w_in"] + K) * 128  # stages: an input row and a weight row each
+    assert p["ring_wrows"] == 0
     slots = p["consumer_warps"] // S
-    assert p["smem_bytes"] == ring + (S - 1) * slots * M * R * 32 * 8  # + partial-sum exchange area
-    tiles = -(-H // p["tile_h"]) * -(-W // p["tile_w"]) * -(-C // 64)
-    assert p["tiles"] == B * tiles
+    red = (S - 1) * slots * M * R * 32 * 8  # partial-sum exchange area
+    tiles_h = -(-H // p["tile_h"])
+    strips = B * -(-W // p["tile_w"]) * -(-C // 64)
+    bt = p["band_tiles"]
+    if bt == 0:  # tile mode: a stage holds an input row and a weight row
+        assert p["ring_rows"] >= p["tile_h"]
+        assert (2 * p["ring_rows"] + 2) * 8 <= 1024  # mbarrier area
+        assert p["smem_bytes"] == 1024 + p["ring_rows"] * (p["tile_w_in"] + K) * 128 + red
+        assert p["tiles"] == strips * tiles_h
+    else:  # band mode (mixed, K <= 17): input rows only, two resident K x K weight buffers
+        assert accum == 1 and K <= 17 and bt >= 1
+        assert p["ring_rows"] >= p["tile_h"] + K - 1
+        assert (2 * p["ring_rows"] + 6) * 8 <= 1024
+        stages = 1024 + p["ring_rows"] * p["tile_w_in"] * 128 + red
+        assert p["smem_bytes"] == -(-stages // 128) * 128 + 2 * K * K * 128
+        assert p["tiles"] == strips * -(-tiles_h // bt)  # bands
     assert 1 <= p["grid"] <= min(p["tiles"], p["ctas_per_sm"] * 148) or (B == 0 and p["grid"] == 0)
 
 
@@ -141,7 +152,7 @@ def test_row_split_candidates_for_small_images():
     splits = {c["row_splits"] for c in small}
     assert {1, 2, 4} <= splits
     for c in small:
-        assert c["consumer_warps"] <= 16 and c["consumer_warps"] % c["row_splits"] == 0
+        assert c["consumer_warps"] <= 31 and c["consumer_warps"] % c["row_splits"] == 0
         assert c["ring_rows"] >= c["tile_h"] + c["row_splits"] - 1 or c["ring_rows"] == c["tile_h"] + 26
     big = _lib.plan_candidates(64, 56, 56, 1024, 9, 1)
     assert {c["row_splits"] for c in big} == {1}

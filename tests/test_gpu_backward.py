@@ -139,5 +139,7 @@ def test_autograd_through_the_fused_op(eng, act):
         gv = to_host(got.grad).astype(np.float64) if got.dim() == 4 else got.grad.cpu().numpy().astype(np.float64)
         rv = ref.grad.numpy()
         rel = np.linalg.norm(gv - rv) / (np.linalg.norm(rv) + 1e-30)
-        assert rel < 5e-3, f"d{name}: rel-L2 {rel:.2e}"
+        # ReLU's derivative jumps at 0: where the fp16 pre-activation and the exact one straddle 0
+        # (|z| within the forward's error) the mask differs, which is the gradient's own conditioning
+        assert rel < (2e-2 if act == "relu" else 5e-3), f"d{name}: rel-L2 {rel:.2e}"
     assert eng.device_error() == 0

@@ -359,3 +359,116 @@ def test_zero_batch_is_noop(eng):
     wd = torch.zeros(7, 7, 64, dtype=torch.float16, device="cuda")
     y = eng.conv2d_nhwc(xd, wd)
     assert y.shape == xd.shape
+
+
+@pytest.mark.parametrize("accum", [0, 1])
+@pytest.mark.parametrize("B,H,W,C,K", [(1, 32, 32, 256, 9), (2, 13, 21, 136, 7), (1, 11, 30, 64, 13), (1, 9, 9, 72, 5)])
+def test_residual_read_from_the_stage_ring(eng, oracle_mod, B, H, W, C, K, accum):
+    """A ConvMixer block's residual is the convolution's input: with one tile per CTA and a ring that
+    holds the whole tile, the epilogue reads it from the staged input rows.  The result must equal,
+    bit for bit, the same plan reading an identical residual tensor from global memory, and the oracle."""
+    from depthwise_conv_b200 import _lib
+    x, w = make_problem(900 + K, B, H, W, C, K)
+    rng = np.random.default_rng(K + 1)
+    bias = (rng.standard_normal(C) * 0.2).astype(np.float16)
+    scale = rng.uniform(0.5, 1.5, C).astype(np.float16)
+    shift = (rng.standard_normal(C) * 0.2).astype(np.float16)
+    exact, _ = oracle_mod.dw_forward(x, w, bias, scale, shift, x, "gelu")
+    xd, wd = to_dev(x), to_dev(w)
+    x_copy = xd.clone()  # same values, another tensor: the global-memory residual path
+    vec = [to_dev(v) for v in (bias, scale, shift)]
+    seen, ran = set(), 0
+    for c in sorted(_lib.plan_candidates(B, H, W, C, K, accum), key=lambda c: c["model_cost"]):
+        key = (c["cols_per_thread"], c["rows_per_thread"], c["row_splits"])
+        if key in seen:
+            continue
+        seen.add(key)
+        plan = dict(c, grid=0, ring_rows=c["tile_h"] + K - 1)
+        try:
+            y_ring = eng.conv2d_nhwc_fused(xd, wd, *vec, xd, "gelu", accum, plan=plan)
+            y_glob = eng.conv2d_nhwc_fused(xd, wd, *vec, x_copy, "gelu", accum, plan=plan)
+        except _lib.DwbError as e:  # a candidate whose full-tile ring or registers do not fit
+            assert e.status == _lib.ERR_BAD_ARG
+            continue
+        torch.cuda.synchronize()
+        assert torch.equal(y_ring, y_glob), f"R={key[0]} M={key[1]} S={key[2]}: ring residual differs"
+        assert_parity(oracle_mod, y_ring, exact, tight=accum == 0, xw=(x, w),
+                      what=f"R={key[0]} M={key[1]} S={key[2]} tile={c['tile_h']}x{c['tile_w']}")
+        ran += 1
+        if ran >= 6:
+            break
+    assert ran >= 2
+    assert eng.device_error() == 0
+
+
+BAND_SHAPES = [(3, 20, 24, 136, 9), (2, 32, 32, 256, 7), (1, 13, 30, 64, 13), (4, 9, 40, 72, 5), (2, 17, 17, 128, 17),
+               (2, 5, 7, 64, 3), (1, 40, 12, 64, 1)]
+
+
+@pytest.mark.parametrize("B,H,W,C,K", BAND_SHAPES)
+def test_band_mode_plans(eng, oracle_mod, B, H, W, C, K):
+    """Band mode (each input row staged once per band, the K x K weights resident and double-buffered
+    across bands): band sizes from 1 tile to the whole image, row splits, M = 2, ragged channel blocks
+    and image edges; one band per CTA, persistent CTAs, and 3 CTAs walking every band (so each CTA's
+    consecutive bands change channel block and the weight buffers alternate)."""
+    from depthwise_conv_b200 import _lib
+    x, w = make_problem(1200 + K, B, H, W, C, K)
+    rng = np.random.default_rng(K + 7)
+    bias = (rng.standard_normal(C) * 0.2).astype(np.float16)
+    scale = rng.uniform(0.5, 1.5, C).astype(np.float16)
+    shift = (rng.standard_normal(C) * 0.2).astype(np.float16)
+    exact, _ = oracle_mod.dw_forward(x, w, bias, scale, shift, x, "gelu")
+    xd, wd = to_dev(x), to_dev(w)
+    vec = [to_dev(v) for v in (bias, scale, shift)]
+    seen, ran = set(), 0
+    cands = [c for c in _lib.plan_candidates(B, H, W, C, K, 1) if c["band_tiles"] > 0]
+    assert cands, "no band-mode candidates"
+    for c in sorted(cands, key=lambda c: c["model_cost"]):
+        key = (c["cols_per_thread"], c["rows_per_thread"], c["row_splits"], c["band_tiles"])
+        if key in seen:
+            continue
+        seen.add(key)
+        for grid in (0, -1, 3):
+            try:
+                y = eng.conv2d_nhwc_fused(xd, wd, *vec, xd, "gelu", 1, plan=dict(c, grid=grid))
+            except _lib.DwbError as e:  # a candidate whose real register count does not fit
+                assert e.status == _lib.ERR_BAD_ARG
+                break
+            torch.cuda.synchronize()
+            assert_parity(oracle_mod, y, exact, tight=False,
+                          what=f"band={key[3]} R={key[0]} M={key[1]} S={key[2]} tile={c['tile_h']}x{c['tile_w']} "
+                               f"ring={c['ring_rows']} grid={grid}")
+            ran += 1
+        if len(seen) >= 8:
+            break
+    assert ran >= 3
+    assert eng.device_error() == 0
+
+
+def test_band_mode_matches_tile_mode_bitwise(eng):
+    """Same variant, same arithmetic: a band plan and the tile plan of the same register block agree bit
+    for bit (only the staging of the rows and weights differs)."""
+    from depthwise_conv_b200 import _lib
+    B, H, W, C, K = 4, 32, 32, 192, 9
+    x, w = make_problem(77, B, H, W, C, K)
+    xd, wd = to_dev(x), to_dev(w)
+    cands = _lib.plan_candidates(B, H, W, C, K, 1)
+    pairs = 0
+    # (row split S = 1: with S > 1 the two modes may deal the kernel rows of an edge tile to the split
+    # groups differently, which changes the order of the fp32 partial-sum additions)
+    for c in sorted((c for c in cands if c["band_tiles"] > 0 and c["row_splits"] == 1),
+                    key=lambda c: c["model_cost"])[:12]:
+        twin = next((t for t in cands if t["band_tiles"] == 0 and all(
+            t[f] == c[f] for f in ("cols_per_thread", "rows_per_thread", "tile_h", "tile_w", "row_splits",
+                                   "load_schedule"))), None)
+        if twin is None:
+            continue
+        try:
+            yb = eng.conv2d_nhwc_fused(xd, wd, accum=1, plan=dict(c, grid=-1))
+            yt = eng.conv2d_nhwc_fused(xd, wd, accum=1, plan=dict(twin, grid=-1))
+        except _lib.DwbError:
+            continue
+        torch.cuda.synchronize()
+        assert torch.equal(yb, yt)
+        pairs += 1
+    assert pairs >= 2

@@ -228,8 +228,23 @@ def test_engine_vs_reference_kernel_same_protocol(cm_ext, rk_ext, name, which, f
         ext = rk_ext
         ref_call = lambda: getattr(ext, fn)(x, w, empty_bias)  # noqa: E731
     ours = lambda: eng.conv2d_nhwc_fused(x, w, out=y)  # noqa: E731
+    # the drop-in module a reference user calls (bench_custom_warm.py:40-60 times modules under no_grad)
+    if which == "cm":
+        mod = eng.depthwise_torch_ops.CustomDepthwiseConv2d(C, K, bias=False).cuda()
+    else:
+        mod = {31: eng.depthwise_replknet_nhwc_ops.NHWCDepthwise31x31_128,
+               29: eng.depthwise_replknet_nhwc_ops.NHWCDepthwise29x29_256,
+               27: eng.depthwise_replknet_nhwc_ops.NHWCDepthwise27x27_512}[K]().cuda()
+        with torch.no_grad():
+            mod.bias.zero_()
+    with torch.no_grad():
+        mod.weight.copy_(w)
+    def module_call():
+        with torch.no_grad():
+            return mod(x)
     res = {"config": name, "B": B, "HW": HW, "C": C, "K": K,
-           "ref_eager_us": _eager_us(ref_call), "ours_eager_us": _eager_us(ours)}
+           "ref_eager_us": _eager_us(ref_call), "ours_eager_us": _eager_us(ours),
+           "ours_module_eager_us": _eager_us(module_call)}
     try:
         res["ref_graph_us"] = _graph_us(ref_call)
     except RuntimeError as e:  # a reference entry point that cannot be captured: eager numbers only
