@@ -319,6 +319,7 @@ def run_dw_configs(args, dev, stream, flush, rank, world, hfma2_tf, only=()):
     import torch
 
     import depthwise_conv_b200 as dwb
+    from depthwise_conv_b200 import _lib
     from depthwise_conv_b200.shard import max_over_ranks, shard_range
 
     peaks = measured_peaks()
@@ -374,6 +375,11 @@ def run_dw_configs(args, dev, stream, flush, rank, world, hfma2_tf, only=()):
                "hbm_bytes_per_gpu": by_gpu,
                "hbm_frac_cold": (by_gpu / (cold * 1e-6) / 1e9 / peaks["hbm_gbs"]) if cold and peaks.get("hbm_gbs")
                else None}
+        if B:
+            pl = _lib.plan_select(B, H, W, C, K)
+            ent["kernel"] = "dw_band_kernel" if pl["band_tiles"] else "dw_stream_kernel"
+            ent["plan"] = {k: pl[k] for k in ("cols_per_thread", "rows_per_thread", "tile_h", "tile_w", "ring_rows",
+                                              "consumer_warps", "grid", "row_splits", "load_schedule", "band_tiles")}
         tr = traffic.get(name)
         if tr is not None:
             ent["dram_traffic"] = tr
@@ -539,7 +545,8 @@ def run_ours(args):
                    "dw_layer": {"B": Bd, "H": H, "W": W, "C": C, "K": K,
                                 "epilogue": "bias+GELU+BN+residual fused",
                                 "plan": {k: plan[k] for k in ("cols_per_thread", "rows_per_thread", "tile_h",
-                                                              "tile_w", "consumer_warps", "accum")}}},
+                                                              "tile_w", "ring_rows", "consumer_warps", "grid",
+                                                              "row_splits", "band_tiles", "accum")}}},
         "e2e": {"value": head["e2e"], "unit": "img/s", "h2d_bytes_per_step": head["h2d"],
                 "d2h_bytes_per_step": head["d2h"]},
         "dw_us_per_layer": dw_us,
@@ -547,7 +554,8 @@ def run_ours(args):
                      "frac": achieved_tf / hfma2_tf, "traffic": traffic,
                      "peak_source": "measured in this run: CUDA-core HFMA2 microbenchmark (dwb_probe_fma_peak); "
                                     "MEASURED_PEAKS.json has no CUDA-core FMA figure",
-                     "kernel": "dw_stream_kernel on 1x32x32x1536 k9 with bias+GELU+BN+residual (the model's DW layer)",
+                     "kernel": ("dw_band_kernel" if plan.get("band_tiles") else "dw_stream_kernel") +
+                               " on 1x32x32x1536 k9 with bias+GELU+BN+residual (the model's DW layer)",
                      "flops_per_launch": fl, "ffma2_peak": ffma2_tf,
                      "hbm": {"achieved": dw_gbs, "peak": peaks.get("hbm_gbs"), "unit": "GB/s",
                              "frac": dw_gbs / peaks["hbm_gbs"] if peaks.get("hbm_gbs") else None,
@@ -728,7 +736,8 @@ def run_dw(args):
                    "parallelism": f"batch-sharded x{world}, no collectives",
                    "l2": "flushed (256 MB write) between timed iterations",
                    "plan": {k: plan[k] for k in ("cols_per_thread", "rows_per_thread", "tile_h", "tile_w",
-                                                 "consumer_warps", "accum")}},
+                                                 "ring_rows", "consumer_warps", "grid", "row_splits", "band_tiles",
+                                                 "accum")}},
         "roofline": {"bound": "fma", "achieved": achieved, "peak": hfma2_tf, "unit": "TFLOP/s",
                      "frac": achieved / hfma2_tf, "flops_per_launch": fl / world,
                      "traffic": profiled_traffic().get(f"dw_{Bg}_{H}_{W}_{C}_{K}"),

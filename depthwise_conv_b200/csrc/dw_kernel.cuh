@@ -473,12 +473,15 @@ __device__ __forceinline__ void dw_stream_body(const CUtensorMap& tmap_x, const 
       wait_s.next(NS);
     }
 
+    bool ready = false;  // this step's stage was found complete during the previous step
     for (int st = 0; st < ti.nsteps && ok; ++st) {
       // stage st + tile_h - 1: the last input row and the weight row of this step
-      ok = mbar_wait_bounded(&full[wait_s.slot], wait_s.phase, p.err, 2);
+      if (!ready) ok = mbar_wait_bounded(&full[wait_s.slot], wait_s.phase, p.err, 2);
       if (!ok) break;
       const __half2* wrow = reinterpret_cast<const __half2*>(ring + wait_s.slot * p.stage_bytes + row_bytes) + lane;
       wait_s.next(NS);
+      // probe the next step's stage now; the answer is read after this step's FMAs
+      ready = st + 1 < ti.nsteps && mbar_test_wait(&full[wait_s.slot], wait_s.phase);
 
       const int s = ti.s_lo + st;  // kernel row
       const int slot1 = (my_slot + 1 == NS) ? 0 : my_slot + 1;
@@ -694,15 +697,19 @@ __device__ __forceinline__ void dw_band_body(const CUtensorMap& tmap_x, const CU
       int turn = sg;
       int my_slot = (band_slot0 + h0rel + trow0) % NS;
 
+      bool ready = false;  // row wait_v was found complete during the previous step
       for (int s = 0; s < K; ++s) {
         const int need = min(h0rel + s + p.tile_h - 1, bi.nv - 1);
         while (wait_v <= need) {
-          ok = mbar_wait_bounded(&full[wait_s.slot], wait_s.phase, p.err, 2);
+          if (!ready) ok = mbar_wait_bounded(&full[wait_s.slot], wait_s.phase, p.err, 2);
+          ready = false;
           if (!ok) break;
           wait_s.next(NS);
           ++wait_v;
         }
         if (!ok) break;
+        // probe the row the next step waits for first; the answer is read after this step's FMAs
+        ready = wait_v < bi.nv && mbar_test_wait(&full[wait_s.slot], wait_s.phase);
         const int slot1 = (my_slot + 1 == NS) ? 0 : my_slot + 1;
         const __half2* xrow0 = reinterpret_cast<const __half2*>(ring + my_slot * p.stage_bytes) + xoff;
         const __half2* xrow1 = reinterpret_cast<const __half2*>(ring + slot1 * p.stage_bytes) + xoff;
