@@ -394,28 +394,44 @@ __device__ __forceinline__ void dw_stream_body(const CUtensorMap& tmap_x, const 
   if (warp == p.consumer_warps) {
     // ---------------- producer warp ----------------
     // Fills the stages in order; a stage is refilled only after every
-    // consumer warp released its previous use (empty barrier).
+    // consumer warp released its previous use (empty barrier).  Fill q of a
+    // tile: its input row (skipped outside the image) and, for q >= tile_h - 1,
+    // the weight row of the step that first needs that input row.
+    auto fill = [&](int slot, const TileInfo& ti, int q) {
+      const int abs_row = ti.h0 - PAD + ti.s_lo + q;
+      unsigned char* dst = ring + slot * p.stage_bytes;
+      const bool xrow = abs_row >= 0 && abs_row < p.H;
+      const bool wrow = q >= p.tile_h - 1;
+      const uint32_t bytes = (xrow ? row_bytes : 0u) + (wrow ? wrow_bytes : 0u);
+      if (bytes) {
+        mbar_arrive_expect_tx(&full[slot], bytes);
+        if (xrow) tma_load_4d(dst, &tmap_x, &full[slot], ti.c0, ti.w0 - PAD, abs_row, ti.b);
+        if (wrow) tma_load_3d(dst + row_bytes, &tmap_w, &full[slot], ti.c0, 0, ti.s_lo + q - (p.tile_h - 1));
+      } else {
+        mbar_arrive(&full[slot]);  // nothing to load (rows above/below the image are skipped)
+      }
+    };
+    // The CTA's first fills find every stage free, so lane q issues fill q of
+    // the first tile: one thread issuing TMA loads back to back waits ~100
+    // clocks per load, and the first compute step needs tile_h of them.
+    int first = 0;
+    if (blockIdx.x < p.num_tiles) {
+      const TileInfo ti = decode_tile<K>(p, blockIdx.x);
+      first = min(min(NS, ti.nrows), 32);
+      if (lane < first) fill(lane, ti, lane);
+    }
+    __syncwarp();
     if (lane == 0) {
       RingPos fr;  // next stage to fill, and the parity of that fill
-      long long fills = 0;
+      for (int i = 0; i < first; ++i) fr.next(NS);
+      long long fills = first;
       bool ok = true;
       for (uint32_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
         const TileInfo ti = decode_tile<K>(p, t);
-        int abs_row = ti.h0 - PAD + ti.s_lo;  // input row of stage 0
-        for (int q = 0; q < ti.nrows; ++q, ++abs_row) {
+        for (int q = (t == blockIdx.x) ? first : 0; q < ti.nrows; ++q) {
           if (fills >= NS) ok = mbar_wait_bounded<kProducerSleeps>(&empty[fr.slot], fr.phase ^ 1u, p.err, 3);
           if (!ok) break;
-          unsigned char* dst = ring + fr.slot * p.stage_bytes;
-          const bool xrow = abs_row >= 0 && abs_row < p.H;
-          const bool wrow = q >= p.tile_h - 1;
-          const uint32_t bytes = (xrow ? row_bytes : 0u) + (wrow ? wrow_bytes : 0u);
-          if (bytes) {
-            mbar_arrive_expect_tx(&full[fr.slot], bytes);
-            if (xrow) tma_load_4d(dst, &tmap_x, &full[fr.slot], ti.c0, ti.w0 - PAD, abs_row, ti.b);
-            if (wrow) tma_load_3d(dst + row_bytes, &tmap_w, &full[fr.slot], ti.c0, 0, ti.s_lo + q - (p.tile_h - 1));
-          } else {
-            mbar_arrive(&full[fr.slot]);  // nothing to load (rows above/below the image are skipped)
-          }
+          fill(fr.slot, ti, q);
           fr.next(NS);
           ++fills;
         }
@@ -623,29 +639,48 @@ __device__ __forceinline__ void dw_band_body(const CUtensorMap& tmap_x, const CU
 
   if (warp == p.consumer_warps) {
     // ---------------- producer warp ----------------
+    auto fill = [&](int slot, const BandInfo& bi, int v) {
+      const int row = bi.h_lo - PAD + v;
+      if (row >= 0 && row < p.H) {
+        mbar_arrive_expect_tx(&full[slot], row_bytes);
+        tma_load_4d(ring + slot * p.stage_bytes, &tmap_x, &full[slot], bi.c0, bi.w0 - PAD, row, bi.b);
+      } else {
+        mbar_arrive(&full[slot]);  // rows above/below the image: nothing to load, never read
+      }
+    };
+    // the CTA's first band: its weights and first rows issued by separate lanes (as in the tile kernel)
+    int first = 0;
+    if (blockIdx.x < p.num_bands) {
+      const BandInfo bi = decode_band<K>(p, blockIdx.x);
+      first = min(min(NS, bi.nv), 31);
+      if (lane == 31) {
+        mbar_arrive_expect_tx(&wfull[0], kWeightBytes);
+        tma_load_3d(smem + p.wbuf_off, &tmap_w, &wfull[0], bi.c0, 0, 0);
+      } else if (lane < first) {
+        fill(lane, bi, lane);
+      }
+    }
+    __syncwarp();
     if (lane == 0) {
       RingPos fr;
-      long long fills = 0;
+      for (int i = 0; i < first; ++i) fr.next(NS);
+      long long fills = first;
       bool ok = true;
       uint32_t it = 0;
       for (uint32_t j = blockIdx.x; j < p.num_bands && ok; j += gridDim.x, ++it) {
         const BandInfo bi = decode_band<K>(p, j);
         const int par = static_cast<int>(it & 1u);
-        // the k-th use of weight buffer par waits until every consumer is done with use k - 1
-        if (it >= 2) ok = mbar_wait_bounded<kProducerSleeps>(&wempty[par], ((it >> 1) - 1) & 1u, p.err, 3);
-        if (!ok) break;
-        mbar_arrive_expect_tx(&wfull[par], kWeightBytes);
-        tma_load_3d(smem + p.wbuf_off + par * kWeightBytes, &tmap_w, &wfull[par], bi.c0, 0, 0);
-        for (int v = 0; v < bi.nv; ++v) {
+        if (it > 0) {
+          // the k-th use of weight buffer par waits until every consumer is done with use k - 1
+          if (it >= 2) ok = mbar_wait_bounded<kProducerSleeps>(&wempty[par], ((it >> 1) - 1) & 1u, p.err, 3);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&wfull[par], kWeightBytes);
+          tma_load_3d(smem + p.wbuf_off + par * kWeightBytes, &tmap_w, &wfull[par], bi.c0, 0, 0);
+        }
+        for (int v = (it == 0) ? first : 0; v < bi.nv; ++v) {
           if (fills >= NS) ok = mbar_wait_bounded<kProducerSleeps>(&empty[fr.slot], fr.phase ^ 1u, p.err, 3);
           if (!ok) break;
-          const int row = bi.h_lo - PAD + v;
-          if (row >= 0 && row < p.H) {
-            mbar_arrive_expect_tx(&full[fr.slot], row_bytes);
-            tma_load_4d(ring + fr.slot * p.stage_bytes, &tmap_x, &full[fr.slot], bi.c0, bi.w0 - PAD, row, bi.b);
-          } else {
-            mbar_arrive(&full[fr.slot]);  // rows above/below the image: nothing to load, never read
-          }
+          fill(fr.slot, bi, v);
           fr.next(NS);
           ++fills;
         }
