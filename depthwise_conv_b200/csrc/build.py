@@ -14,10 +14,10 @@ thread in steps (64, 72, 80, 96, 128, 168, 255 registers = 8 ... 2 warps per
 sub-partition), and ptxas's own choice often lands above a step it could reach
 with no or almost no spilling.  ``--regcaps`` compiles every kernel variant
 uncapped and then at each step below its natural count (``__maxnreg__``),
-reads the registers and spill bytes ptxas reports, and caps each variant at
-the lowest step where it spills at most 16 bytes of stores and 16 bytes of
-loads (a few loop-invariant words).  The result is ``dw_regcaps.inc``,
-committed with the sources; a plain build uses it.
+reads the registers and spill bytes ptxas reports, and picks a cap per variant
+(``choose_caps``: a near-step rule for all, a low-spill rule for K <= 13).
+The result is ``dw_regcaps.inc``, committed with the sources; a plain build
+uses it.
 """
 from __future__ import annotations
 
@@ -128,18 +128,29 @@ def _ptxas_report(src: str, extra: list[str]) -> dict:
 def choose_caps(reports: dict) -> dict:
     """reports: {cap (255 = uncapped): {variant: (regs, spill stores, spill loads)}} -> {variant: cap}.
 
-    The lowest step below the uncapped count whose spills stay within the allowance; 255 (no cap)
-    when no step qualifies."""
+    Near-step rule: a variant at most 10 registers above a step is capped at that step if it then
+    spills at most 32 bytes of stores.  Low-spill rule (K <= 13 only): the lowest step below the
+    uncapped count whose spills stay within 16 bytes of stores and 16 of loads.  A variant takes
+    the lower cap of the rules that apply (255 = no cap).  Measured on B200: the low-spill rule
+    gains the small kernels a warp per sub-partition (k9 R16: 128 -> 96 registers), while the
+    large ones, already FMA-bound with 4 warps, lost 2-3% under it."""
     caps = {}
     for key, (natural, _, _) in reports[255].items():
-        caps[key] = 255
-        for step in _STEPS:
-            if step >= natural or step not in reports or key not in reports[step]:
-                continue
-            regs, st, ld = reports[step][key]
-            if regs <= step and st <= _SPILL_STORES_OK and ld <= _SPILL_LOADS_OK:
-                caps[key] = step
-                break
+        cap = 255
+        step = max((b for b in _STEPS if b <= natural), default=None)
+        if step is not None and step < natural <= step + 10 and step in reports and key in reports[step]:
+            regs, st, _ = reports[step][key]
+            if regs <= step and st <= 32:
+                cap = step
+        if key[0] <= 13:
+            for low in _STEPS:
+                if low >= natural or low not in reports or key not in reports[low]:
+                    continue
+                regs, st, ld = reports[low][key]
+                if regs <= low and st <= _SPILL_STORES_OK and ld <= _SPILL_LOADS_OK:
+                    cap = min(cap, low)
+                    break
+        caps[key] = cap
     return caps
 
 

@@ -71,6 +71,9 @@ constexpr int kPixelBytes = kChannelsPerCta * 2;    // one staged pixel = 128 B
 constexpr int kPixelH2 = kChannelsPerCta / 2;       // half2 per staged pixel
 constexpr int kBarrierBytes = 1024;                 // mbarrier area at smem start
 constexpr bool kProducerSleeps = true;              // producer's empty-slot waits may suspend
+// Consumers' stage waits spin on try_wait: letting them suspend as the producer does (leaving
+// the issue slots to computing warps) measured 0-5% slower on B200.
+constexpr bool kConsumerSleeps = false;
 
 struct DwParams {
   __half* y;
@@ -485,14 +488,14 @@ __device__ __forceinline__ void dw_stream_body(const CUtensorMap& tmap_x, const 
 
     // Stages [0, tile_h - 1) hold input rows that step 0 needs as well.
     for (int q = 0; q < p.tile_h - 1 && ok; ++q) {
-      ok = mbar_wait_bounded(&full[wait_s.slot], wait_s.phase, p.err, 1);
+      ok = mbar_wait_bounded<kConsumerSleeps>(&full[wait_s.slot], wait_s.phase, p.err, 1);
       wait_s.next(NS);
     }
 
     bool ready = false;  // this step's stage was found complete during the previous step
     for (int st = 0; st < ti.nsteps && ok; ++st) {
       // stage st + tile_h - 1: the last input row and the weight row of this step
-      if (!ready) ok = mbar_wait_bounded(&full[wait_s.slot], wait_s.phase, p.err, 2);
+      if (!ready) ok = mbar_wait_bounded<kConsumerSleeps>(&full[wait_s.slot], wait_s.phase, p.err, 2);
       if (!ok) break;
       const __half2* wrow = reinterpret_cast<const __half2*>(ring + wait_s.slot * p.stage_bytes + row_bytes) + lane;
       wait_s.next(NS);
@@ -714,7 +717,7 @@ __device__ __forceinline__ void dw_band_body(const CUtensorMap& tmap_x, const CU
       bias_c0 = bi.c0;
       load_channel_params(p, bi.c0, lane, bias, scale, shift);
     }
-    ok = mbar_wait_bounded(&wfull[par], (it >> 1) & 1u, p.err, 1);
+    ok = mbar_wait_bounded<kConsumerSleeps>(&wfull[par], (it >> 1) & 1u, p.err, 1);
     if (!ok) break;
     const __half2* wbase = reinterpret_cast<const __half2*>(smem + p.wbuf_off + par * kWeightBytes) + lane;
     const int band_slot0 = wait_s.slot;  // every row of the previous band was waited for and released
@@ -736,7 +739,7 @@ __device__ __forceinline__ void dw_band_body(const CUtensorMap& tmap_x, const CU
       for (int s = 0; s < K; ++s) {
         const int need = min(h0rel + s + p.tile_h - 1, bi.nv - 1);
         while (wait_v <= need) {
-          if (!ready) ok = mbar_wait_bounded(&full[wait_s.slot], wait_s.phase, p.err, 2);
+          if (!ready) ok = mbar_wait_bounded<kConsumerSleeps>(&full[wait_s.slot], wait_s.phase, p.err, 2);
           ready = false;
           if (!ok) break;
           wait_s.next(NS);

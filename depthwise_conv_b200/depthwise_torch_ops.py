@@ -121,12 +121,15 @@ def _depthwise_conv2d_32_1536_13_fake(input, weight):
     return torch.empty_like(input)
 
 
-_FIXED_IMPL = {
-    'depthwise::conv2d_32_1536_9': _depthwise_conv2d_32_1536_9_impl,
-    'depthwise::conv2d_32_1536_9_v2': _depthwise_conv2d_32_1536_9_v2_impl,
-    'depthwise::conv2d_32_768_7': _depthwise_conv2d_32_768_7_impl,
-    'depthwise::conv2d_16_1536_9': _depthwise_conv2d_16_1536_9_impl,
-    'depthwise::conv2d_32_1536_13': _depthwise_conv2d_32_1536_13_impl,
+# (op name) -> the C entry point and fixed shape its "default" impl launches; the modules call
+# _fixed_op with these directly in eager inference (torch.library.impl used as a decorator does not
+# return the function, so the impls above cannot be called by name)
+_FIXED_ARGS = {
+    'depthwise::conv2d_32_1536_9': ("dwb_depthwise_forward_32_1536_9", 32, 32, 1536, 9, True),
+    'depthwise::conv2d_32_1536_9_v2': ("dwb_depthwise_forward_32_1536_9_v2", 32, 32, 1536, 9, True),
+    'depthwise::conv2d_32_768_7': ("dwb_depthwise_forward_32_768_7", 32, 32, 768, 7, False),
+    'depthwise::conv2d_16_1536_9': ("dwb_depthwise_forward_16_1536_9", 16, 16, 1536, 9, False),
+    'depthwise::conv2d_32_1536_13': ("dwb_depthwise_forward_32_1536_13", 32, 32, 1536, 13, False),
 }
 
 
@@ -185,7 +188,8 @@ class CustomDepthwiseConv2d(nn.Module):
             # (the same kernel launch; torch.compile and autograd keep going through the ops)
             if self.bias is not None or self.op_name == 'depthwise::conv2d_nhwc':
                 return dw_ops.conv2d_nhwc_fused(x, self.weight, bias=self.bias)
-            return _FIXED_IMPL[self.op_name](x, self.weight)
+            fn, H_, W_, C_, K_, stride = _FIXED_ARGS[self.op_name]
+            return _fixed_op(fn, x, self.weight, H_, W_, C_, K_, stride)
         if self.bias is not None or self.op_name == 'depthwise::conv2d_nhwc':
             # bias fused into the kernel epilogue (one launch instead of conv + add)
             return torch.ops.depthwise.conv2d_nhwc(x, self.weight, self.bias)

@@ -188,3 +188,15 @@ def test_stem_keeps_the_convolution_for_overlapping_patches(eng):
     from depthwise_conv_b200.convmixer import FusedStem
     assert FusedStem(nn.Conv2d(3, 16, 7, stride=4), "gelu", nn.BatchNorm2d(16).eval()).patch == 0
     assert FusedStem(nn.Conv2d(3, 16, 7, stride=7, padding=1), "gelu", nn.BatchNorm2d(16).eval()).patch == 0
+
+
+def test_module_direct_path_covers_every_fixed_op():
+    """In eager inference CustomDepthwiseConv2d calls the fixed-shape launchers itself; every op it can
+    select has its entry point and shape listed."""
+    from depthwise_conv_b200 import depthwise_torch_ops as m
+    for op in set(m.CustomDepthwiseConv2d.SUPPORTED_CONFIGS.values()) | {"depthwise::conv2d_32_1536_9_v2"}:
+        fn, H, W, C, K, stride = m._FIXED_ARGS[op]
+        assert fn.startswith("dwb_depthwise_forward_")
+        # the op name spells the shape: conv2d_<HW>_<C>_<K>[_v2]
+        hw, c, k = (int(v) for v in op.split("::conv2d_")[1].split("_")[:3])
+        assert (H, W, C, K) == (hw, hw, c, k) and stride == (C == 1536 and K == 9 and H == 32)
