@@ -13,7 +13,7 @@ import threading
 PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(PKG_DIR, "libdwconv_b200.so")
 
-ABI_VERSION = 5  # DWB_ABI_VERSION of include/dwconv_b200.h
+ABI_VERSION = 6  # DWB_ABI_VERSION of include/dwconv_b200.h
 
 # dwb_status
 OK = 0
@@ -83,6 +83,7 @@ SIGNATURES = {
     "dwb_depthwise_29x29_256_nhwc": ([_p, _p, _p, _p, _i, _i, _i, _i, _p], _i),
     "dwb_depthwise_27x27_512_nhwc": ([_p, _p, _p, _p, _i, _i, _i, _i, _p], _i),
     "dwb_bias_act_affine_nhwc": ([_p, _p, _p, _p, _p, _i64, _i64, _i, _p], _i),
+    "dwb_pointwise_conv_nhwc": ([_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _p], _i),
     "dwb_device_error": ([ctypes.POINTER(ctypes.c_int), _i, _p], _i),
     "dwb_probe_fma_peak": ([ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double), _p], _i),
     "dwb_selftest_bounded_wait": ([_i64, _p], _i),
@@ -182,7 +183,8 @@ class DeviceTimeoutError(RuntimeError):
 # Codes a kernel stores in the device error word (csrc/dw_device.cuh).
 DEVICE_ERROR_CODES = {1: "stage wait before a tile's first step", 2: "stage wait of a step",
                       3: "producer's free-stage wait", 4: "row-split partial-sum hand-off",
-                      5: "bounded-wait self-test"}
+                      5: "bounded-wait self-test", 6: "pointwise GEMM producer's free-stage wait",
+                      7: "pointwise GEMM operand wait", 8: "pointwise GEMM accumulator wait"}
 
 
 def after_launch(stream: int, where: str) -> None:

@@ -20,6 +20,7 @@
 #include "dw_kernel.cuh"
 #include "dw_launch.h"
 #include "dw_planner.h"
+#include "dw_pointwise_gemm.h"
 
 namespace dwb {
 
@@ -632,6 +633,109 @@ int dwb_conv2d_nhwc_bwd_weight(const void* x, const void* dy, float* dw, int64_t
   if (ce != cudaSuccess) {
     (void)cudaGetLastError();
     return cuda_fail("cudaLaunchKernelExC(dw_wgrad_kernel)", ce);
+  }
+  return DWB_OK;
+}
+
+// ---- pointwise block: the fused 1x1-convolution GEMM -------------------------------------
+// [rows][cols] fp16 row-major matrix as a 2-D TMA tensor; box = kPwTileK columns (128 bytes) x
+// box_rows rows with the 128-byte swizzle the MMA's shared-memory descriptors describe.
+static int encode_matrix_map(CUtensorMap* m, const void* base, long long rows, long long cols, int box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return driver_fail("cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)", -1);
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
+  const cuuint32_t box[2] = {(cuuint32_t)kPwTileK, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? DWB_OK : driver_fail("cuTensorMapEncodeTiled(matrix)", static_cast<int>(r));
+}
+
+static bool pw_tile_n_compiled(int bn) {
+  for (int v : kPwTileNs)
+    if (v == bn) return true;
+  return false;
+}
+
+// Output channels per tile for an M x N product on `sms` SMs (one CTA per SM): the fewest
+// waves of tiles, each costing its BN columns of MMAs plus a fixed ~32-column-equivalent of
+// fill and epilogue latency.
+static int pw_choose_tile_n(long long M, long long N, int sms) {
+  int best = kPwTileNs[0];
+  double best_cost = 0.0;
+  for (int bn : kPwTileNs) {
+    const long long tiles = ((M + kPwTileM - 1) / kPwTileM) * ((N + bn - 1) / bn);
+    const long long waves = (tiles + sms - 1) / sms;
+    const double cost = static_cast<double>(waves) * (bn + 32.0);
+    if (best_cost == 0.0 || cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+int dwb_pointwise_conv_nhwc(const void* x, const void* w, const void* bias, const void* scale, const void* shift,
+                            void* y, int64_t pixels, int64_t C_in, int64_t C_out, int act, int tile_n,
+                            void* stream) {
+  if (act < DWB_ACT_NONE || act > DWB_ACT_GELU) return DWB_ERR_BAD_ARG;
+  if (tile_n != 0 && !pw_tile_n_compiled(tile_n)) return DWB_ERR_BAD_ARG;
+  if (pixels < 0 || C_in < 8 || (C_in % 8) != 0 || C_out < 8 || (C_out % 8) != 0) return DWB_ERR_BAD_SHAPE;
+  if (pixels > 0x7fffff00LL || C_in > (1LL << 24) || C_out > 65535LL * kPwTileNs[0]) return DWB_ERR_BAD_SHAPE;
+  if (pixels == 0) return DWB_OK;
+  if (!x || !w || !y) return DWB_ERR_NULL_POINTER;
+  if (!aligned(x, 16) || !aligned(w, 16) || !aligned(y, 16) || (bias && !aligned(bias, 2)) ||
+      (scale && !aligned(scale, 2)) || (shift && !aligned(shift, 2)))
+    return DWB_ERR_BAD_ALIGN;
+  DeviceState* st = nullptr;
+  int rc = get_device_state(&st);
+  if (rc != DWB_OK) return rc;
+  const int bn = tile_n ? tile_n : pw_choose_tile_n(pixels, C_out, st->hw.sm_count);
+  if ((C_out + bn - 1) / bn > 65535) return DWB_ERR_BAD_SHAPE;
+  const void* fn = pw_gemm_kernel_for(bn, act);
+  if (!fn) return DWB_ERR_UNSUPPORTED;
+
+  PwGemmParams p;
+  p.bias = static_cast<const __half*>(bias);
+  p.scale = static_cast<const __half*>(scale);
+  p.shift = static_cast<const __half*>(shift);
+  p.y = static_cast<__half*>(y);
+  p.M = static_cast<int>(pixels);
+  p.N = static_cast<int>(C_out);
+  p.K = static_cast<int>(C_in);
+  p.num_kb = static_cast<int>((C_in + kPwTileK - 1) / kPwTileK);
+  int stages = std::min(kPwMaxStages, std::max(2, p.num_kb));
+  while (stages > 2 && pw_smem_bytes(bn, stages) > st->hw.smem_optin) --stages;
+  if (pw_smem_bytes(bn, stages) > st->hw.smem_optin) return DWB_ERR_UNSUPPORTED;
+  p.stages = stages;
+  p.err = st->err_word;
+  const int smem = pw_smem_bytes(bn, stages);
+  {
+    static int smem_set[kMaxDevices][4][3];  // largest dynamic smem allowed so far: device, tile_n, act
+    int dev = 0, bi = 0;
+    cudaGetDevice(&dev);
+    while (kPwTileNs[bi] != bn) ++bi;
+    std::lock_guard<std::mutex> lk(st->mu);
+    if (smem_set[dev][bi][act] < smem) {
+      const cudaError_t ce = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (ce != cudaSuccess) return cuda_fail("cudaFuncSetAttribute(pw_gemm_kernel)", ce);
+      smem_set[dev][bi][act] = smem;
+    }
+  }
+  CUtensorMap tmx, tmw;
+  rc = encode_matrix_map(&tmx, x, pixels, C_in, kPwTileM);
+  if (rc != DWB_OK) return rc;
+  rc = encode_matrix_map(&tmw, w, C_out, C_in, bn);
+  if (rc != DWB_OK) return rc;
+  void* args[3] = {&tmx, &tmw, &p};
+  const dim3 grid(static_cast<unsigned>((pixels + kPwTileM - 1) / kPwTileM), static_cast<unsigned>((C_out + bn - 1) / bn));
+  const cudaError_t ce = launch_kernel(fn, grid, dim3(kPwThreads), args, static_cast<size_t>(smem),
+                                       static_cast<cudaStream_t>(stream));
+  if (ce != cudaSuccess) {
+    (void)cudaGetLastError();
+    return cuda_fail("cudaLaunchKernelExC(pw_gemm_kernel)", ce);
   }
   return DWB_OK;
 }

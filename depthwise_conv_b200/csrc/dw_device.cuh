@@ -14,7 +14,9 @@ namespace dwb {
 // when one of its bounded waits expires: 1 = stage wait before a tile's
 // first step, 2 = stage wait of a step, 3 = producer's free-stage (empty)
 // wait, 4 = row-split partial-sum hand-off, 5 = the bounded-wait self-test
-// (dwb_selftest_bounded_wait), whose wait nothing ever completes.  The word lives in the launcher's
+// (dwb_selftest_bounded_wait), whose wait nothing ever completes; the
+// pointwise GEMM: 6 = producer's free-stage wait, 7 = MMA issuer's operand
+// wait, 8 = epilogue's accumulator wait.  The word lives in the launcher's
 // translation unit; kernels receive its address.
 
 // ~1 s at 2 GHz: far above any legitimate wait (a row load takes ~1 us).

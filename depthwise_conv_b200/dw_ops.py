@@ -163,6 +163,54 @@ def bias_act_affine(x: torch.Tensor, bias=None, scale=None, shift=None, act: int
     return y
 
 
+def pointwise_gemm(a: torch.Tensor, w: torch.Tensor, bias=None, scale=None, shift=None, act: int | str = 0,
+                   out: torch.Tensor | None = None, tile_n: int = 0) -> torch.Tensor:
+    """y = act(a @ w^T + bias) * scale + shift as one tensor-core kernel (``dwb_pointwise_conv_nhwc``).
+
+    ``a``: [M, K] fp16 CUDA, row-major (the NHWC pixels of a channels_last tensor, or a patch
+    matrix); ``w``: [N, K] fp16 row-major (a 1x1 convolution's weight as PyTorch stores it);
+    bias/scale/shift: [N] or None.  Returns [M, N] fp16 (NHWC pixels x output channels);
+    accumulation in fp32.  ``tile_n`` forces the output-channel tile (64, 96, 128, 256).
+    """
+    if not a.is_cuda or a.dtype != torch.float16 or a.dim() != 2 or not a.is_contiguous():
+        raise RuntimeError(f"input must be a contiguous float16 CUDA matrix [M, K], got {tuple(a.shape)}")
+    if w.dim() == 4 and w.shape[2:] == (1, 1):
+        w = w.reshape(w.shape[0], w.shape[1])
+    if not w.is_cuda or w.dtype != torch.float16 or w.dim() != 2 or w.shape[1] != a.shape[1] or not w.is_contiguous():
+        raise RuntimeError(f"weight must be a contiguous float16 CUDA matrix [N, K={a.shape[1]}], got {tuple(w.shape)}")
+    if w.device != a.device:
+        raise RuntimeError(f"weight is on {w.device}, input on {a.device}")
+    M, K = a.shape
+    N = w.shape[0]
+    act_code = ACT_CODES[act] if isinstance(act, str) else int(act)
+    bp = check_vec(bias, N, "bias", a.device)
+    sp = check_vec(scale, N, "scale", a.device)
+    hp = check_vec(shift, N, "shift", a.device)
+    if out is None:
+        y = torch.empty((M, N), dtype=torch.float16, device=a.device)
+    else:
+        if not out.is_cuda or out.dtype != torch.float16 or out.shape != (M, N) or not out.is_contiguous():
+            raise RuntimeError(f"out must be a contiguous float16 CUDA matrix [{M}, {N}]")
+        y = out
+    with _DeviceGuard(a.device):
+        stream = _stream_of(a)
+        _lib.call("dwb_pointwise_conv_nhwc", a.data_ptr(), w.data_ptr(), bp or None, sp or None, hp or None,
+                  y.data_ptr(), M, K, N, act_code, int(tile_n), stream)
+        _lib.after_launch(stream, "depthwise pointwise_gemm")
+    return y
+
+
+def pointwise_conv_nhwc(x: torch.Tensor, w: torch.Tensor, bias=None, scale=None, shift=None,
+                        act: int | str = 0) -> torch.Tensor:
+    """A 1x1 convolution with its bias, activation and BN fold on a channels_last fp16 tensor
+    [B, C_in, H, W]; ``w``: [C_out, C_in] (or [C_out, C_in, 1, 1]).  Returns channels_last
+    [B, C_out, H, W] -- the pixel matrix needs no layout change on either side."""
+    check_input(x)
+    B, C, H, W = x.shape
+    z = pointwise_gemm(x.permute(0, 2, 3, 1).reshape(B * H * W, C), w, bias, scale, shift, act)
+    return z.view(B, H, W, -1).permute(0, 3, 1, 2)
+
+
 def weight_rot180(w: torch.Tensor) -> torch.Tensor:
     """[K, K, C] taps rotated by 180 degrees (the input-gradient filter)."""
     C = w.shape[2]
@@ -218,6 +266,10 @@ torch.library.define(
     "depthwise::bias_act_affine",
     "(Tensor input, Tensor? bias, Tensor? scale, Tensor? shift, int act) -> Tensor",
 )
+torch.library.define(
+    "depthwise::pointwise_gemm",
+    "(Tensor input, Tensor weight, Tensor? bias, Tensor? scale, Tensor? shift, int act) -> Tensor",
+)
 
 
 @torch.library.impl("depthwise::conv2d_nhwc", "default")
@@ -248,6 +300,16 @@ def _bias_act_affine_impl(input, bias, scale, shift, act):
 @torch.library.register_fake("depthwise::bias_act_affine")
 def _bias_act_affine_fake(input, bias, scale, shift, act):
     return torch.empty_like(input)
+
+
+@torch.library.impl("depthwise::pointwise_gemm", "default")
+def _pointwise_gemm_impl(input, weight, bias, scale, shift, act):
+    return pointwise_gemm(input, weight, bias, scale, shift, act)
+
+
+@torch.library.register_fake("depthwise::pointwise_gemm")
+def _pointwise_gemm_fake(input, weight, bias, scale, shift, act):
+    return input.new_empty((input.shape[0], weight.shape[0]))
 
 
 def _conv2d_nhwc_setup(ctx, inputs, output):

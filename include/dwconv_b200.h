@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define DWB_ABI_VERSION 5
+#define DWB_ABI_VERSION 6
 
 #if defined(__GNUC__)
 #define DWB_API __attribute__((visibility("default")))
@@ -170,6 +170,22 @@ DWB_API int dwb_conv2d_nhwc_fwd_planned(const void* x, const void* w, const void
 DWB_API int dwb_bias_act_affine_nhwc(const void* x, const void* bias, const void* scale,
                                      const void* shift, void* y, int64_t pixels, int64_t C,
                                      int act, void* stream);
+
+/* y = act(x * w^T + bias) * scale + shift: a whole ConvMixer pointwise block
+ * (1x1 conv -> bias -> act -> BatchNorm, convmixer/convmixer.py:116-118), or a
+ * patch stem given its patch matrix, as one tensor-core kernel (tcgen05 MMAs
+ * into tensor memory, the epilogue applied on the way out; no intermediate in
+ * HBM).  x: [pixels][C_in] fp16 row-major (NHWC activations), w: [C_out][C_in]
+ * fp16 row-major (the 1x1 weight as PyTorch stores it), y: [pixels][C_out]
+ * fp16; bias/scale/shift: [C_out] fp16 or NULL.  C_in, C_out multiples of 8,
+ * x / w / y 16-byte aligned, y must not overlap x or w.  fp32 accumulation.
+ * tile_n: output channels per CTA tile (64, 96, 128 or 256), 0 = chosen by
+ * the launcher.  In the reference these are PyTorch's conv2d (cuDNN), bias,
+ * GELU and BatchNorm kernels; there is no reference entry point to replace. */
+DWB_API int dwb_pointwise_conv_nhwc(const void* x, const void* w, const void* bias,
+                                    const void* scale, const void* shift, void* y,
+                                    int64_t pixels, int64_t C_in, int64_t C_out, int act,
+                                    int tile_n, void* stream);
 
 /* ---- reference-facing entry points --------------------------------------
  * One per launcher of luckychen/depthwise_conv on this path, with the same

@@ -39,7 +39,7 @@ def test_every_declared_symbol_is_exported_and_bound(lib):
 
 def test_abi_version_and_status_strings(lib):
     from depthwise_conv_b200 import _lib
-    assert lib.dwb_abi_version() == 5
+    assert lib.dwb_abi_version() == 6
     for code in range(9):
         assert lib.dwb_status_string(code) and b"unknown" not in lib.dwb_status_string(code)
     assert lib.dwb_status_string(99) == b"unknown status"
