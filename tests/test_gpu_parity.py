@@ -472,3 +472,29 @@ def test_band_mode_matches_tile_mode_bitwise(eng):
         assert torch.equal(yb, yt)
         pairs += 1
     assert pairs >= 2
+
+
+def _tuned_entries():
+    """(B, H, W, C, K) of every measured plan in the library's tuned table (mixed accumulation)."""
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "depthwise_conv_b200", "csrc",
+                        "dw_tuned_plans.inc")
+    out = []
+    for ln in open(path):
+        ln = ln.strip()
+        if ln.startswith("{"):
+            v = [int(t) for t in ln.strip("{},").split(",")]
+            if v[5] == 1:
+                out.append(tuple(v[:5]) + (tuple(v[6:]),))
+    return out
+
+
+@pytest.mark.parametrize("B,H,W,C,K,fields", _tuned_entries(),
+                         ids=[f"{b}x{h}x{w}x{c}_k{k}" for b, h, w, c, k, _ in _tuned_entries()])
+def test_every_tuned_plan(eng, oracle_mod, B, H, W, C, K, fields):
+    """The tuner times plans without checking them: run each table entry's own problem (the launcher
+    picks exactly that plan) against the oracle at sampled pixels and by channel sums."""
+    from depthwise_conv_b200 import _lib
+    plan = _lib.plan_select(B, H, W, C, K)
+    names = ("cols_per_thread", "rows_per_thread", "tile_h", "tile_w", "ring_rows")
+    assert tuple(plan[n] for n in names) == fields[:5], (plan, fields)
+    _sampled_check(eng, oracle_mod, B, H, W, C, K, npix=256, seed=B * 7 + K)
