@@ -23,6 +23,8 @@ import time
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 TABLE = os.path.join(HERE, "csrc", "dw_tuned_plans.inc")
+# plans for a ConvMixer block (residual = the input), used by launches whose residual is their input
+TABLE_RES = os.path.join(HERE, "csrc", "dw_tuned_plans_res.inc")
 
 DEFAULT_PROBLEMS = [
     (1, 32, 32, 768, 7), (1, 32, 32, 1536, 9), (1, 16, 16, 1536, 9), (1, 32, 32, 1536, 13),
@@ -137,13 +139,16 @@ def tune_problem(B, H, W, C, K, accum, budget, proxy_batch=8, finalists=8):
     return default, best
 
 
-def write_table(rows, path):
+def write_table(rows, path, base=TABLE):
+    """Merge ``rows`` into the committed table ``base`` (its comment header kept) and write it to ``path``."""
     lines = ["// dw_tuned_plans.inc -- plans measured fastest on B200 by depthwise_conv_b200/tune.py.",
              "// {B, H, W, C, K, accum, R, M, tile_h, tile_w, ring_rows, ring_wrows, grid(-1 persistent, 0 one tile/CTA),",
              "//  row_splits, load_schedule, band_tiles (0 = tile mode)}"]
     old = []
-    if os.path.exists(TABLE):  # start from the committed table
-        for ln in open(TABLE):
+    if os.path.exists(base):  # start from the committed table
+        head = [ln.rstrip("\n") for ln in open(base) if ln.startswith("//")]
+        lines = head or lines
+        for ln in open(base):
             ln = ln.strip()
             if ln.startswith("{"):
                 old.append(ln)
@@ -166,15 +171,18 @@ def main():
     ap.add_argument("--accum", choices=["mixed", "f32"], default="mixed")
     ap.add_argument("--proxy-batch", type=int, default=8, help="images per timing while ranking candidates")
     ap.add_argument("--finalists", type=int, default=8, help="plans re-timed on the full batch")
-    ap.add_argument("--epilogue", choices=["none", "gelu_bn", "gelu_bn_res"], default="none",
+    ap.add_argument("--epilogue", choices=["none", "gelu_bn", "gelu_bn_res", "relu_bn_res"], default="none",
                     help="time with the fused epilogue a model uses (bias+GELU+BN, + residual = input)")
     ap.add_argument("--no-write", action="store_true")
-    ap.add_argument("--out", default=TABLE, help="where to write the merged table (default: the library's)")
+    ap.add_argument("--out", default=None,
+                    help="where to write the merged table (default: the library's; the ConvMixer-block table for "
+                         "the *_res epilogues)")
     args = ap.parse_args()
     from depthwise_conv_b200 import _lib
     accum = _lib.ACCUM_MIXED if args.accum == "mixed" else _lib.ACCUM_F32
     if args.epilogue != "none":
-        EPILOGUE.update(act="gelu", residual=args.epilogue == "gelu_bn_res")
+        EPILOGUE.update(act="relu" if args.epilogue.startswith("relu") else "gelu",
+                        residual=args.epilogue.endswith("_res"))
     probs = [tuple(int(v) for v in p.split(",")) for p in args.problems] or DEFAULT_PROBLEMS
     rows = []
     for B, H, W, C, K in probs:
@@ -184,8 +192,10 @@ def main():
         if plan is not None:
             rows.append(((B, H, W, C, K, accum), plan))
     if not args.no_write:
-        write_table(rows, args.out)
-        print("wrote", args.out)
+        base = TABLE_RES if args.epilogue.endswith("_res") else TABLE
+        out = args.out or base
+        write_table(rows, out, base)
+        print("wrote", out)
 
 
 if __name__ == "__main__":

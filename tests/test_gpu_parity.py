@@ -474,10 +474,10 @@ def test_band_mode_matches_tile_mode_bitwise(eng):
     assert pairs >= 2
 
 
-def _tuned_entries():
-    """(B, H, W, C, K) of every measured plan in the library's tuned table (mixed accumulation)."""
+def _tuned_entries(name="dw_tuned_plans.inc"):
+    """(B, H, W, C, K) of every measured plan in one of the library's tuned tables (mixed accumulation)."""
     path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "depthwise_conv_b200", "csrc",
-                        "dw_tuned_plans.inc")
+                        name)
     out = []
     for ln in open(path):
         ln = ln.strip()
@@ -498,3 +498,20 @@ def test_every_tuned_plan(eng, oracle_mod, B, H, W, C, K, fields):
     names = ("cols_per_thread", "rows_per_thread", "tile_h", "tile_w", "ring_rows")
     assert tuple(plan[n] for n in names) == fields[:5], (plan, fields)
     _sampled_check(eng, oracle_mod, B, H, W, C, K, npix=256, seed=B * 7 + K)
+
+
+@pytest.mark.parametrize("B,H,W,C,K,fields", _tuned_entries("dw_tuned_plans_res.inc"),
+                         ids=[f"{b}x{h}x{w}x{c}_k{k}" for b, h, w, c, k, _ in _tuned_entries("dw_tuned_plans_res.inc")])
+@pytest.mark.parametrize("act", ["gelu", "relu"])
+def test_every_convmixer_block_plan(eng, oracle_mod, B, H, W, C, K, fields, act):
+    """The ConvMixer-block table (used when the residual is the input): each entry's problem with the full
+    epilogue and residual = input, against the oracle."""
+    x, w = make_problem(B * 11 + K, B, H, W, C, K)
+    rng = np.random.default_rng(K)
+    bias = (rng.standard_normal(C) * 0.1).astype(np.float16)
+    scale = rng.uniform(0.5, 1.5, C).astype(np.float16)
+    shift = (rng.standard_normal(C) * 0.1).astype(np.float16)
+    y = run_engine(eng, x, w, bias, scale, shift, True, act, 1)
+    exact, _ = oracle_mod.dw_forward(x, w, bias, scale, shift, x, act)
+    max_err, rel = oracle_mod.parity(to_host(y).astype(np.float64), exact)
+    assert max_err <= MAX_TOL and rel <= REL_TOL, f"max {max_err:.3e} rel {rel:.3e}"
