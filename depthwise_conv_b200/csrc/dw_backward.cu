@@ -59,8 +59,8 @@ __global__ void __launch_bounds__(160, 1) dw_wgrad_kernel(const __grid_constant_
     fence_mbar_init();
   }
   __syncthreads();
-  griddep_launch_dependents();
   griddep_wait();  // x and dy may come from the previous kernel
+  griddep_launch_dependents();
 
   const int c0 = blockIdx.x * 64;
   const int kh = blockIdx.y;
@@ -139,8 +139,8 @@ __global__ void __launch_bounds__(160, 1) dw_wgrad_kernel(const __grid_constant_
 
 // w_rot[kh][kw][c] = w[K-1-kh][K-1-kw][c], 8 channels (16 bytes) per thread.
 __global__ void weight_rot180_kernel(const uint4* __restrict__ w, uint4* __restrict__ wr, int K, int C8) {
-  griddep_launch_dependents();
   griddep_wait();
+  griddep_launch_dependents();
   const int n = K * K * C8;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const int c8 = i % C8;

@@ -121,8 +121,13 @@ struct RingPos {
 // stream has finished; griddep_wait() returns once that kernel has completed
 // and its memory is visible, so every global read or write of data another
 // kernel may produce comes after it.  griddep_launch_dependents() lets the
-// next kernel of the stream start its own set-up early.  Both are no-ops for
-// a kernel launched without the attribute.
+// next kernel of the stream start its own set-up early.  Every engine kernel
+// calls it right after its own wait, not before: signalled before the wait,
+// each waiting kernel let the next one in as well, and a graph of many
+// back-to-back launches of a small grid piled up generations of resident,
+// waiting CTAs (7x7x1024 k13: 3.8 us per launch in a graph of 50, 6.6 us in
+// one of 1000; 3.4 us flat with the call after the wait).  Both are no-ops
+// for a kernel launched without the attribute.
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 

@@ -390,9 +390,10 @@ __device__ __forceinline__ void dw_stream_body(const CUtensorMap& tmap_x, const 
   }
   __syncthreads();
   // Everything above overlaps the previous kernel of the stream (programmatic
-  // dependent launch); from here on the kernel reads and writes global memory.
-  griddep_launch_dependents();
+  // dependent launch); from here on the kernel reads and writes global memory,
+  // and the next kernel may start its own set-up.
   griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == p.consumer_warps) {
     // ---------------- producer warp ----------------
@@ -637,8 +638,8 @@ __device__ __forceinline__ void dw_band_body(const CUtensorMap& tmap_x, const CU
     fence_mbar_init();
   }
   __syncthreads();
-  griddep_launch_dependents();
   griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == p.consumer_warps) {
     // ---------------- producer warp ----------------

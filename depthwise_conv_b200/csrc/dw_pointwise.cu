@@ -35,8 +35,8 @@ __global__ void __launch_bounds__(256) bias_act_affine_kernel(const uint4* __res
                                                               const __half* __restrict__ scale,
                                                               const __half* __restrict__ shift, uint4* __restrict__ y,
                                                               long long groups, int cgroups) {
-  griddep_launch_dependents();
   griddep_wait();  // x may be the previous kernel's output (programmatic dependent launch)
+  griddep_launch_dependents();
   const int stride = static_cast<int>(gridDim.x * blockDim.x);  // the launcher keeps the grid below 2^31 threads
   const int g0 = static_cast<int>(blockIdx.x * blockDim.x + threadIdx.x);
   // channel group of the current vector, advanced by stride mod cgroups per

@@ -111,8 +111,8 @@ __global__ void __launch_bounds__(kPwThreads, 1)
   const uint32_t tmem = *tmem_slot;
   // Set-up above overlaps the previous kernel of the stream; global memory
   // (x may be its output, y may alias what it reads) only after the wait.
-  griddep_launch_dependents();
   griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 4) {
     // ---------------- TMA producer ----------------
