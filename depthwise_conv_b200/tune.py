@@ -9,9 +9,12 @@ graph of back-to-back launches, best of 3) on a proxy batch of at most
 fastest few are then timed on the full batch (both load schedules, both grid
 modes) and the winner is written to ``csrc/dw_tuned_plans.inc``, which the
 library consults before its cost model (rebuild afterwards).  ``--epilogue``
-times the fused op with the epilogue a model uses (the table is keyed by
-shape only, so tune a shape for the epilogue it is mostly run with).  Results
-are also printed as JSON lines.
+times the fused op with the epilogue a model uses; with a residual
+(``gelu_bn_res``, ``relu_bn_res``: the residual is the input, a ConvMixer
+block) the winner goes to ``csrc/dw_tuned_plans_res.inc``, which the library
+consults first for launches whose residual is their input.  A plan only
+enters a table when it beats the plan the library would use without it.
+Results are also printed as JSON lines.
 """
 from __future__ import annotations
 
