@@ -90,6 +90,8 @@ SIGNATURES = {
     "dwb_weight_rot180": ([_p, _p, _i64, _i, _p], _i),
     "dwb_conv2d_nhwc_bwd_data": ([_p, _p, _p, _i64, _i64, _i64, _i64, _i, _p], _i),
     "dwb_conv2d_nhwc_bwd_weight": ([_p, _p, _p, _i64, _i64, _i64, _i64, _i, _p], _i),
+    "dwb_conv2d_nhwc_bwd_weight_workspace": ([_i64, _i64, _i64, _i64, _i, ctypes.POINTER(_i64)], _i),
+    "dwb_conv2d_nhwc_bwd_weight_det": ([_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i, _p], _i),
     "dwb_conv2d_nhwc_bwd_data_noalloc": ([_p, _p, _p, _i64, _i64, _i64, _i64, _i, _p], _i),
 }
 

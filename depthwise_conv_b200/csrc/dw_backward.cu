@@ -128,6 +128,14 @@ __global__ void __launch_bounds__(160, 1) dw_wgrad_kernel(const __grid_constant_
   }
   const int c = c0 + 2 * lane;
   if (!ok || c >= p.C) return;
+  if (p.partial) {  // deterministic: this warp's own slice, summed in order by wgrad_reduce_kernel
+    const long long slice = static_cast<long long>(blockIdx.z) * p.consumer_warps + warp;
+    float* out = p.partial + (slice * K + kh) * K * p.C + c;
+#pragma unroll
+    for (int kw = 0; kw < K; ++kw)
+      *reinterpret_cast<float2*>(out + static_cast<long long>(kw) * p.C) = bits_f2(acc[kw]);
+    return;
+  }
   float* out = p.dw + static_cast<long long>(kh) * K * p.C + c;
 #pragma unroll
   for (int kw = 0; kw < K; ++kw) {
@@ -136,6 +144,26 @@ __global__ void __launch_bounds__(160, 1) dw_wgrad_kernel(const __grid_constant_
     atomicAdd(out + static_cast<long long>(kw) * p.C + 1, v.y);
   }
 }
+
+__global__ void __launch_bounds__(256) wgrad_reduce_kernel(const float4* __restrict__ partial, float4* __restrict__ dw,
+                                                           long long n4, int slices) {
+  griddep_wait();  // the partial sums come from the previous kernel
+  griddep_launch_dependents();
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    float4 a = dw[i];
+    for (int s = 0; s < slices; ++s) {  // fixed order: the same bits on every run
+      const float4 v = partial[static_cast<long long>(s) * n4 + i];
+      a.x += v.x;
+      a.y += v.y;
+      a.z += v.z;
+      a.w += v.w;
+    }
+    dw[i] = a;
+  }
+}
+
+const void* wgrad_reduce_kernel_fn() { return reinterpret_cast<const void*>(&wgrad_reduce_kernel); }
 
 // w_rot[kh][kw][c] = w[K-1-kh][K-1-kw][c], 8 channels (16 bytes) per thread.
 __global__ void weight_rot180_kernel(const uint4* __restrict__ w, uint4* __restrict__ wr, int K, int C8) {

@@ -16,6 +16,8 @@ struct WgradParams {
   int stages;                 // ring depth
   uint32_t ring_off;          // byte offset of stage 0 in dynamic smem
   uint32_t stage_bytes;       // (2 tile_w + K - 1) * 128
+  float* partial;             // deterministic mode: [gridDim.z * consumer_warps][K][K][C] partial sums,
+                              // one slice per (row chunk, column tile, warp); nullptr: atomics into dw
   int* err;                   // device error word
 };
 
@@ -23,5 +25,9 @@ constexpr int kWgradColumnsPerWarp = 16;
 
 // dw_wgrad_kernel<K> for an odd K in 1..31 (nullptr otherwise).
 const void* wgrad_kernel_for(int K);
+
+// dw[i] += sum over slices s = 0..slices-1 of partial[s][i], in slice order, for i < n
+// (the deterministic weight gradient's reduction; n a multiple of 4).
+const void* wgrad_reduce_kernel_fn();
 
 }  // namespace dwb

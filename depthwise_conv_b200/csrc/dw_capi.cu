@@ -579,33 +579,45 @@ int dwb_conv2d_nhwc_bwd_data(const void* dy, const void* w_rot180, void* dx, int
                         DWB_ACCUM_DEFAULT, stream);
 }
 
-int dwb_conv2d_nhwc_bwd_weight(const void* x, const void* dy, float* dw, int64_t B, int64_t H, int64_t W,
-                               int64_t C, int K, void* stream) {
-  if (B < 0 || H < 1 || W < 1 || C < 8 || (C % 8) != 0 || K < 1 || K > 31 || (K % 2) == 0)
-    return DWB_ERR_BAD_SHAPE;
+// Grid of the weight-gradient kernel: CTA = (64 channels, kernel row, column tile, chunk of rows);
+// up to 4 consumer warps of 16 columns; chunks sized for ~4 CTAs per SM.
+struct WgradGeometry {
+  int ncw, tile_w;
+  long long col_tiles, cblocks, chunks, rows_per_chunk;
+};
+static int wgrad_geometry(long long B, long long H, long long W, long long C, int K, int sm_count, WgradGeometry* g) {
+  if (B < 0 || H < 1 || W < 1 || C < 8 || (C % 8) != 0 || K < 1 || K > 31 || (K % 2) == 0) return DWB_ERR_BAD_SHAPE;
   if (H > (1 << 30) || W > (1 << 30) || C > (1 << 30) || B > (1 << 30)) return DWB_ERR_BAD_SHAPE;
-  if (B == 0) return DWB_OK;
-  if (!x || !dy || !dw) return DWB_ERR_NULL_POINTER;
-  if (!aligned(x, 16) || !aligned(dy, 16) || !aligned(dw, 8)) return DWB_ERR_BAD_ALIGN;
+  g->ncw = static_cast<int>(std::min<long long>(4, (W + kWgradColumnsPerWarp - 1) / kWgradColumnsPerWarp));
+  g->tile_w = g->ncw * kWgradColumnsPerWarp;
+  g->col_tiles = (W + g->tile_w - 1) / g->tile_w;
+  g->cblocks = (C + kChannelsPerCta - 1) / kChannelsPerCta;
+  const long long rows = std::max<long long>(1, B * H);
+  const long long base = g->cblocks * K * g->col_tiles;
+  long long chunks = (4LL * sm_count + base - 1) / base;
+  chunks = std::max<long long>(1, std::min(chunks, rows));
+  g->rows_per_chunk = (rows + chunks - 1) / chunks;
+  g->chunks = (rows + g->rows_per_chunk - 1) / g->rows_per_chunk;
+  if (g->cblocks > 0x7fffffffLL || g->col_tiles * g->chunks > 65535) return DWB_ERR_BAD_SHAPE;
+  return DWB_OK;
+}
+
+// The deterministic mode's workspace: one fp32 [K][K][C] slice per (row chunk, column tile, warp).
+static long long wgrad_workspace_bytes(const WgradGeometry& g, long long C, int K) {
+  return g.col_tiles * g.chunks * g.ncw * static_cast<long long>(K) * K * C * 4;
+}
+
+static int launch_wgrad(const void* x, const void* dy, float* dw, void* workspace, long long workspace_bytes,
+                        long long B, long long H, long long W, long long C, int K, void* stream) {
   DeviceState* st = nullptr;
   int rc = get_device_state(&st);
   if (rc != DWB_OK) return rc;
+  WgradGeometry g;
+  rc = wgrad_geometry(B, H, W, C, K, st->hw.sm_count, &g);
+  if (rc != DWB_OK || B == 0) return rc;
   const void* fn = wgrad_kernel_for(K);
   if (!fn) return DWB_ERR_UNSUPPORTED;
-
-  // CTA = (64 channels, kernel row, column tile, chunk of rows); up to 4 consumer warps of 16
-  // columns; chunks sized for ~4 CTAs per SM.
-  const int ncw = static_cast<int>(std::min<long long>(4, (W + kWgradColumnsPerWarp - 1) / kWgradColumnsPerWarp));
-  const int tile_w = ncw * kWgradColumnsPerWarp;
-  const long long col_tiles = (W + tile_w - 1) / tile_w;
-  const long long cblocks = (C + kChannelsPerCta - 1) / kChannelsPerCta;
-  const long long rows = B * H;
-  const long long base = cblocks * K * col_tiles;
-  long long chunks = (4LL * st->hw.sm_count + base - 1) / base;
-  chunks = std::max<long long>(1, std::min(chunks, rows));
-  const long long rows_per_chunk = (rows + chunks - 1) / chunks;
-  chunks = (rows + rows_per_chunk - 1) / rows_per_chunk;
-  if (cblocks > 0x7fffffffLL || col_tiles * chunks > 65535) return DWB_ERR_BAD_SHAPE;
+  if (workspace && workspace_bytes < wgrad_workspace_bytes(g, C, K)) return DWB_ERR_BAD_ARG;
 
   WgradParams p;
   p.dw = dw;
@@ -613,13 +625,14 @@ int dwb_conv2d_nhwc_bwd_weight(const void* x, const void* dy, float* dw, int64_t
   p.H = static_cast<int>(H);
   p.W = static_cast<int>(W);
   p.C = static_cast<int>(C);
-  p.tile_w = tile_w;
-  p.col_tiles = static_cast<int>(col_tiles);
-  p.rows_per_chunk = rows_per_chunk;
-  p.consumer_warps = ncw;
+  p.tile_w = g.tile_w;
+  p.col_tiles = static_cast<int>(g.col_tiles);
+  p.rows_per_chunk = g.rows_per_chunk;
+  p.consumer_warps = g.ncw;
   p.stages = 4;
   p.ring_off = kBarrierBytes;
-  p.stage_bytes = static_cast<uint32_t>(2 * tile_w + K - 1) * kPixelBytes;
+  p.stage_bytes = static_cast<uint32_t>(2 * g.tile_w + K - 1) * kPixelBytes;
+  p.partial = static_cast<float*>(workspace);
   p.err = st->err_word;
   const int smem = static_cast<int>(p.ring_off + p.stages * p.stage_bytes);
   {
@@ -634,19 +647,64 @@ int dwb_conv2d_nhwc_bwd_weight(const void* x, const void* dy, float* dw, int64_t
     }
   }
   CUtensorMap tmx, tmdy;
-  rc = encode_x_map(&tmx, x, B, H, W, C, tile_w + K - 1);
+  rc = encode_x_map(&tmx, x, B, H, W, C, g.tile_w + K - 1);
   if (rc != DWB_OK) return rc;
-  rc = encode_x_map(&tmdy, dy, B, H, W, C, tile_w);
+  rc = encode_x_map(&tmdy, dy, B, H, W, C, g.tile_w);
   if (rc != DWB_OK) return rc;
   void* args[3] = {&tmx, &tmdy, &p};
-  const cudaError_t ce = launch_kernel(fn, dim3(static_cast<unsigned>(cblocks), K, static_cast<unsigned>(col_tiles * chunks)),
-                                       dim3(32 * (ncw + 1)), args, static_cast<size_t>(smem),
-                                       static_cast<cudaStream_t>(stream));
+  cudaError_t ce = launch_kernel(fn, dim3(static_cast<unsigned>(g.cblocks), K, static_cast<unsigned>(g.col_tiles * g.chunks)),
+                                 dim3(32 * (g.ncw + 1)), args, static_cast<size_t>(smem), static_cast<cudaStream_t>(stream));
   if (ce != cudaSuccess) {
     (void)cudaGetLastError();
     return cuda_fail("cudaLaunchKernelExC(dw_wgrad_kernel)", ce);
   }
+  if (workspace) {  // the slices, summed in a fixed order
+    const float4* part = static_cast<const float4*>(workspace);
+    float4* out = reinterpret_cast<float4*>(dw);
+    long long n4 = static_cast<long long>(K) * K * C / 4;
+    int slices = static_cast<int>(g.col_tiles * g.chunks * g.ncw);
+    const long long want = (n4 + 255) / 256;
+    const unsigned blocks = static_cast<unsigned>(std::min<long long>(want, 8LL * st->hw.sm_count));
+    void* rargs[4] = {&part, &out, &n4, &slices};
+    ce = launch_kernel(wgrad_reduce_kernel_fn(), dim3(blocks), dim3(256), rargs, 0, static_cast<cudaStream_t>(stream));
+    if (ce != cudaSuccess) {
+      (void)cudaGetLastError();
+      return cuda_fail("cudaLaunchKernelExC(wgrad_reduce_kernel)", ce);
+    }
+  }
   return DWB_OK;
+}
+
+int dwb_conv2d_nhwc_bwd_weight(const void* x, const void* dy, float* dw, int64_t B, int64_t H, int64_t W,
+                               int64_t C, int K, void* stream) {
+  if (B < 0 || H < 1 || W < 1 || C < 8 || (C % 8) != 0 || K < 1 || K > 31 || (K % 2) == 0)
+    return DWB_ERR_BAD_SHAPE;
+  if (B == 0) return DWB_OK;
+  if (!x || !dy || !dw) return DWB_ERR_NULL_POINTER;
+  if (!aligned(x, 16) || !aligned(dy, 16) || !aligned(dw, 8)) return DWB_ERR_BAD_ALIGN;
+  return launch_wgrad(x, dy, dw, nullptr, 0, B, H, W, C, K, stream);
+}
+
+int dwb_conv2d_nhwc_bwd_weight_workspace(int64_t B, int64_t H, int64_t W, int64_t C, int K, int64_t* bytes) {
+  if (!bytes) return DWB_ERR_NULL_POINTER;
+  DeviceState* st = nullptr;
+  int rc = get_device_state(&st);
+  if (rc != DWB_OK) return rc;
+  WgradGeometry g;
+  rc = wgrad_geometry(B, H, W, C, K, st->hw.sm_count, &g);
+  if (rc != DWB_OK) return rc;
+  *bytes = B == 0 ? 0 : wgrad_workspace_bytes(g, C, K);
+  return DWB_OK;
+}
+
+int dwb_conv2d_nhwc_bwd_weight_det(const void* x, const void* dy, float* dw, void* workspace, int64_t workspace_bytes,
+                                   int64_t B, int64_t H, int64_t W, int64_t C, int K, void* stream) {
+  if (B < 0 || H < 1 || W < 1 || C < 8 || (C % 8) != 0 || K < 1 || K > 31 || (K % 2) == 0)
+    return DWB_ERR_BAD_SHAPE;
+  if (B == 0) return DWB_OK;
+  if (!x || !dy || !dw || !workspace) return DWB_ERR_NULL_POINTER;
+  if (!aligned(x, 16) || !aligned(dy, 16) || !aligned(dw, 16) || !aligned(workspace, 16)) return DWB_ERR_BAD_ALIGN;
+  return launch_wgrad(x, dy, dw, workspace, workspace_bytes, B, H, W, C, K, stream);
 }
 
 // ---- pointwise block: the fused 1x1-convolution GEMM -------------------------------------

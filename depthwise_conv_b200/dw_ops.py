@@ -235,17 +235,31 @@ def conv2d_nhwc_backward_input(dy: torch.Tensor, w: torch.Tensor) -> torch.Tenso
     return dx
 
 
-def conv2d_nhwc_backward_weight(x: torch.Tensor, dy: torch.Tensor, K: int) -> torch.Tensor:
-    """dw of y = conv(x, w) as [K, K, C] float32 (summed over the batch and the image)."""
+def conv2d_nhwc_backward_weight(x: torch.Tensor, dy: torch.Tensor, K: int, deterministic: bool | None = None
+                                ) -> torch.Tensor:
+    """dw of y = conv(x, w) as [K, K, C] float32 (summed over the batch and the image).
+
+    ``deterministic`` (default: ``torch.are_deterministic_algorithms_enabled()``) sums the partial
+    sums in a fixed order through a workspace instead of adding them atomically, so repeated calls
+    give the same bits."""
     check_input(x)
     check_input(dy, "grad_output")
     if dy.shape != x.shape:
         raise RuntimeError(f"grad_output shape {tuple(dy.shape)} != input shape {tuple(x.shape)}")
     B, C, H, W = x.shape
+    if deterministic is None:
+        deterministic = torch.are_deterministic_algorithms_enabled()
     dw = torch.zeros((K, K, C), dtype=torch.float32, device=x.device)
     with _DeviceGuard(x.device):
-        _lib.call("dwb_conv2d_nhwc_bwd_weight", x.data_ptr(), dy.data_ptr(), dw.data_ptr(), B, H, W, C, K,
-                  _stream_of(x))
+        if deterministic:
+            nbytes = ctypes.c_int64(0)
+            _lib.call("dwb_conv2d_nhwc_bwd_weight_workspace", B, H, W, C, K, ctypes.byref(nbytes))
+            ws = torch.empty(max(16, nbytes.value), dtype=torch.uint8, device=x.device)
+            _lib.call("dwb_conv2d_nhwc_bwd_weight_det", x.data_ptr(), dy.data_ptr(), dw.data_ptr(), ws.data_ptr(),
+                      nbytes.value, B, H, W, C, K, _stream_of(x))
+        else:
+            _lib.call("dwb_conv2d_nhwc_bwd_weight", x.data_ptr(), dy.data_ptr(), dw.data_ptr(), B, H, W, C, K,
+                      _stream_of(x))
         _lib.after_launch(_stream_of(x), "depthwise conv2d_nhwc weight gradient")
     return dw
 

@@ -258,6 +258,19 @@ DWB_API int dwb_conv2d_nhwc_bwd_data(const void* dy, const void* w_rot180, void*
 DWB_API int dwb_conv2d_nhwc_bwd_weight(const void* x, const void* dy, float* dw, int64_t B, int64_t H, int64_t W,
                                        int64_t C, int K, void* stream);
 
+/* The weight gradient with a fixed summation order (the same bits on every
+ * run, as torch.use_deterministic_algorithms asks): every CTA warp writes its
+ * partial sums to its own slice of `workspace` (fp32, 16-byte aligned, at
+ * least the size dwb_conv2d_nhwc_bwd_weight_workspace reports for the
+ * problem on the current device) instead of adding them into dw atomically,
+ * and a second kernel adds the slices into dw in slice order.  dw: [K][K][C]
+ * fp32, 16-byte aligned, accumulated into as by dwb_conv2d_nhwc_bwd_weight. */
+DWB_API int dwb_conv2d_nhwc_bwd_weight_workspace(int64_t B, int64_t H, int64_t W, int64_t C, int K,
+                                                 int64_t* bytes);
+DWB_API int dwb_conv2d_nhwc_bwd_weight_det(const void* x, const void* dy, float* dw, void* workspace,
+                                           int64_t workspace_bytes, int64_t B, int64_t H, int64_t W,
+                                           int64_t C, int K, void* stream);
+
 /* Input gradient that allocates nothing (no counterpart in the reference): the
  * same result as dwb_weight_rot180 + dwb_conv2d_nhwc_bwd_data, for callers
  * that cannot allocate device memory where they need it (a serving loop with

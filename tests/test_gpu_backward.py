@@ -143,3 +143,48 @@ def test_autograd_through_the_fused_op(eng, act):
         # (|z| within the forward's error) the mask differs, which is the gradient's own conditioning
         assert rel < (2e-2 if act == "relu" else 5e-3), f"d{name}: rel-L2 {rel:.2e}"
     assert eng.device_error() == 0
+
+
+@pytest.mark.parametrize("B,H,W,C,K", SHAPES + [(8, 56, 56, 1024, 7)])
+def test_deterministic_weight_gradient(eng, oracle_mod, B, H, W, C, K):
+    """The fixed-order mode: the oracle's bar, and the same bits on every run (the atomic mode's
+    partial sums land in any order)."""
+    if B * H * W * C > (1 << 22):  # the large case: repeatability only, the oracle would take minutes
+        rng = np.random.default_rng(K)
+        xd = torch.from_numpy(rng.standard_normal((B, H, W, C)).astype(np.float16)).cuda().permute(0, 3, 1, 2)
+        dyd = torch.from_numpy(rng.standard_normal((B, H, W, C)).astype(np.float16)).cuda().permute(0, 3, 1, 2)
+        dw_exact = None
+    else:
+        x, w, dy = _problem(B, H, W, C, K)
+        _, dw_exact, _ = oracle_mod.dw_backward_numpy(x, w, dy)
+        xd, dyd = to_dev(x), to_dev(dy)
+    runs = [eng.dw_ops.conv2d_nhwc_backward_weight(xd, dyd, K, deterministic=True) for _ in range(3)]
+    torch.cuda.synchronize()
+    assert all(torch.equal(runs[0], r) for r in runs[1:])
+    fast = eng.dw_ops.conv2d_nhwc_backward_weight(xd, dyd, K, deterministic=False)
+    torch.cuda.synchronize()
+    scale = fast.abs().max().item() + 1e-30
+    assert (runs[0] - fast).abs().max().item() <= 1e-5 * scale + 1e-6
+    if dw_exact is not None:
+        got = runs[0].cpu().numpy().astype(np.float64)
+        assert np.abs(got - dw_exact).max() <= 1e-5 * (np.abs(dw_exact).max() + 1e-30) + 1e-6
+
+
+def test_autograd_weight_gradient_follows_torch_determinism(eng):
+    """Under torch.use_deterministic_algorithms(True) the op's backward takes the fixed-order path."""
+    rng = np.random.default_rng(3)
+    x = torch.from_numpy(rng.standard_normal((4, 32, 32, 256)).astype(np.float16)).cuda().permute(0, 3, 1, 2)
+    w = torch.from_numpy((rng.standard_normal((9, 9, 256)) / 9).astype(np.float16)).cuda()
+    prev = torch.are_deterministic_algorithms_enabled()
+    torch.use_deterministic_algorithms(True, warn_only=True)
+    try:
+        grads = []
+        for _ in range(3):
+            wr = w.clone().requires_grad_(True)
+            y = torch.ops.depthwise.conv2d_nhwc(x, wr)
+            y.float().square().sum().backward()
+            grads.append(wr.grad.clone())
+        torch.cuda.synchronize()
+    finally:
+        torch.use_deterministic_algorithms(prev)
+    assert all(torch.equal(grads[0], g) for g in grads[1:])
