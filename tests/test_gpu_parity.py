@@ -515,3 +515,36 @@ def test_every_convmixer_block_plan(eng, oracle_mod, B, H, W, C, K, fields, act)
     exact, _ = oracle_mod.dw_forward(x, w, bias, scale, shift, x, act)
     max_err, rel = oracle_mod.parity(to_host(y).astype(np.float64), exact)
     assert max_err <= MAX_TOL and rel <= REL_TOL, f"max {max_err:.3e} rel {rel:.3e}"
+
+
+def _random_cases(n=120, seed=2024):
+    """Seeded random problems: odd K 1..31, ragged H and W (1..70), C a multiple of 8 (8..264),
+    B 1..3, a random epilogue (activation, bias/scale/shift, residual) and both accumulations."""
+    rng = np.random.default_rng(seed)
+    out = []
+    for i in range(n):
+        K = int(rng.choice(np.arange(1, 32, 2)))
+        H, W = int(rng.integers(1, 71)), int(rng.integers(1, 71))
+        C = 8 * int(rng.integers(1, 34))
+        B = int(rng.integers(1, 4))
+        act = ["none", "relu", "gelu"][int(rng.integers(0, 3))]
+        out.append((i, B, H, W, C, K, act, bool(rng.integers(0, 2)), bool(rng.integers(0, 2)), int(rng.integers(0, 2))))
+    return out
+
+
+@pytest.mark.parametrize("i,B,H,W,C,K,act,with_params,residual,accum", _random_cases(),
+                         ids=[f"r{c[0]}_{c[1]}x{c[2]}x{c[3]}x{c[4]}_k{c[5]}" for c in _random_cases()])
+def test_random_problems(eng, oracle_mod, i, B, H, W, C, K, act, with_params, residual, accum):
+    """Whatever plan the launcher picks for an arbitrary shape meets the oracle's bar."""
+    x, w = make_problem(7000 + i, B, H, W, C, K)
+    rng = np.random.default_rng(i)
+    bias = scale = shift = None
+    if with_params:
+        bias = (rng.standard_normal(C) * 0.2).astype(np.float16)
+        scale = rng.uniform(0.5, 1.5, C).astype(np.float16)
+        shift = (rng.standard_normal(C) * 0.2).astype(np.float16)
+    y = run_engine(eng, x, w, bias, scale, shift, residual, act, accum)
+    exact, _ = oracle_mod.dw_forward(x, w, bias, scale, shift, x if residual else None, act)
+    max_err, rel = oracle_mod.parity(to_host(y).astype(np.float64), exact)
+    assert max_err <= MAX_TOL and rel <= REL_TOL, f"max {max_err:.3e} rel {rel:.3e}"
+    assert eng.device_error() == 0
