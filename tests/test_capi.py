@@ -182,3 +182,15 @@ def test_register_cap_table_is_consistent():
         assert R in (7, 8, 14, 16) or (R in (28, 32) and K <= 13)
         assert pre == 0 or acc == 1  # the read-ahead schedule exists in mixed mode only
         assert cap in (64, 72, 80, 96, 128, 168)
+
+
+def test_plans_respect_hardware_limits_on_random_problems():
+    """The same invariants over seeded random problems the fixed list does not reach."""
+    import numpy as np
+    rng = np.random.default_rng(11)
+    for _ in range(400):
+        K = int(rng.choice(np.arange(1, 32, 2)))
+        H, W = int(rng.integers(1, 601)), int(rng.integers(1, 601))
+        C = 8 * int(rng.integers(1, 513))
+        B = int(rng.choice([1, 2, 3, 8, 33, 512]))
+        test_plans_respect_hardware_limits(B, H, W, C, K, int(rng.integers(0, 2)))
